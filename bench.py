@@ -1,0 +1,353 @@
+"""Decode benchmark of the B200 Qwen2.5 path.
+
+A step is one batch-1 greedy decode token of full-depth Qwen2.5-1.5B (28
+layers, FP32 seeded weights by default) inside a 512-token-prompt, 256-token
+decode window: the prompt is prefilled once (untimed), then steps cycle over
+positions 512..767 (each 256-step segment restarts from the post-prompt state).
+
+  value : device-timed tokens/s -- chained whole-token CUDA-graph replays, the
+          device feeding each top-1 back as the next token, CUDA events on the
+          library stream, max over ranks, summed over ranks (weak scaling:
+          one independent session per GPU, no collective on the data path).
+  e2e   : the same steps through the public C API (qwen_advance): per step one
+          pinned host->device copy of the token state, one graph replay and one
+          device->host read of the top-2, host synchronised every step.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+       [--config fp32-ctx512 | bf16-ctx4096 | fp32-2layer]
+Under torchrun (N > 1) every rank runs its own replica; rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Qwen2.5-1.5B decode tok/s/GPU (bs1, bs64) + % HBM roofline; max |Δlogit|"
+
+CONFIGS = {
+    # Full Qwen2.5-1.5B, native FP32 weights, 512-token prompt, 256 greedy steps.
+    "fp32-ctx512": dict(layers=28, profile=0, prompt=512, window=256),
+    # Full Qwen2.5-1.5B, source-BF16 weights, 4096-token prompt, 512 greedy steps.
+    "bf16-ctx4096": dict(layers=28, profile=2, prompt=4096, window=512),
+    # The reduced 2-layer model of the reference's CPU-runnable case (64 + 32).
+    "fp32-2layer": dict(layers=2, profile=0, prompt=64, window=32),
+}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+        return world, rank, local, dist, torch
+    return 1, 0, local, None, None
+
+
+def barrier(dist, torch):
+    if dist:
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def max_over_ranks(value: float, dist, torch) -> float:
+    if not dist:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prompt_tokens(seed: int, n: int, vocab: int):
+    import numpy as np
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+# ---------------------------------------------------------------- CPU baseline (reference path)
+def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: int | None = None):
+    """The reference's own CPU FP32 C path (src/qwen.c + tests/gpu_stub.c, built
+    from its sources into oracle/_ref), one session per host thread, each
+    decoding from a 2-token prompt; returns (tokens/s, threads, sample, kind,
+    the first thread's logits per step)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import ctypes
+    import numpy as np
+    import cmachine_b200 as cm
+    from checkers import ORACLE, REF_CPU, load
+    path, kind = (REF_CPU, "reference") if REF_CPU.exists() else (ORACLE, "port")
+    L = load(path)
+    shape = cm.qwen_shape(layers, 4096)
+    model = L.orc_model_create(ctypes.byref(shape), 2026, ctypes.byref(cm.BENCH_LAW), int(bf16))
+    n = threads or max(1, min(os.cpu_count() or 1, 32))
+    per_token = 1.3 * layers / 28 + 0.05
+    steps = max(2, int(seconds / max(per_token, 1e-3)) // 1)
+    steps = min(steps, 12 if layers > 2 else 64)
+    results, first_logits = [0] * n, []
+
+    def worker(i):
+        s = L.orc_session_create(model, 64)
+        top = cm.Top2()
+        toks = prompt_tokens(90 + i, 2, shape.vocab)
+        out = np.empty(shape.vocab, np.float32)
+        for t in toks:
+            L.orc_push(s, t, ctypes.byref(top), ctypes.c_void_p(out.ctypes.data))
+        done = len(toks)
+        for _ in range(steps):
+            L.orc_push(s, top.first, ctypes.byref(top), ctypes.c_void_p(out.ctypes.data))
+            if i == 0:
+                first_logits.append(out.copy())
+            done += 1
+        results[i] = done
+        L.orc_session_free(s)
+
+    t0 = time.perf_counter()
+    pool = [threading.Thread(target=worker, args=(i,)) for i in range(n)]
+    for th in pool:
+        th.start()
+    for th in pool:
+        th.join()
+    wall = time.perf_counter() - t0
+    L.orc_model_free(model)
+    total = sum(results)
+    sample = (f"{n} threads x (2-token prompt + {steps} greedy decode steps, every push counted), {layers}-layer "
+              f"{'BF16' if bf16 else 'FP32'} seeded model, one session per thread")
+    return total / wall, n, sample, kind, first_logits
+
+
+def gpu_dlogit(layers: int, profile: int, ref_logits):
+    """max |delta logit| of the GPU path on the CPU sample's first thread."""
+    import numpy as np
+    import cmachine_b200 as cm
+    if not ref_logits:
+        return None
+    model = cm.Model(cm.qwen_shape(layers, 4096), 2026, cm.BENCH_LAW, profile)
+    s = cm.Session(model, 64)
+    worst = 0.0
+    for t in prompt_tokens(90, 2, model.shape.vocab):
+        s.push(t)
+    for ref in ref_logits:
+        s.push(s.pending)
+        worst = max(worst, float(np.max(np.abs(s.logits() - ref))))
+    s.free()
+    model.free()
+    return worst
+
+
+# ---------------------------------------------------------------- B200 arm
+def run_b200(args, cfg, world, rank, local, dist, torch):
+    import cmachine_b200 as cm
+    L = cm.lib()
+    L.qwen_b200_set_device(local)
+    shape = cm.qwen_shape(cfg["layers"], 32768)
+    model = cm.Model(shape, 2026 + rank, cm.BENCH_LAW, cfg["profile"])
+    capacity = cfg["prompt"] + cfg["window"] + 1
+    s = cm.Session(model, capacity)
+    for t in prompt_tokens(7 + rank, cfg["prompt"], shape.vocab):
+        assert s.push(t) == 0
+    status, ckpt = s.checkpoint()
+    assert status == 0
+    p0, pos0, window = s.pending, s.position, cfg["window"]
+    runner = s.runner
+    per_token_launches = L.qwen_b200_launches_per_token(runner)
+
+    def enqueue_steps(k):
+        while k > 0:
+            n = min(k, window)
+            assert L.qwen_b200_enqueue(runner, p0, pos0, n) == 0
+            k -= n
+
+    # Warm-up, then exactly K timed chained steps.
+    enqueue_steps(max(args.warmup, 3))
+    L.gpu_sync()
+    barrier(dist, torch)
+    with ClockSampler(local) as clocks:
+        L.qwen_b200_mark(0)
+        enqueue_steps(args.steps)
+        L.qwen_b200_mark(1)
+        L.gpu_sync()
+        device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    barrier(dist, torch)
+    top = cm.Top2()
+    assert L.qwen_b200_last(runner, top) == 0
+    device_ms = max_over_ranks(device_ms, dist, torch)
+
+    # End to end through qwen_advance (host round trip every step).
+    assert s.restore(ckpt) == 0
+    for _ in range(max(args.warmup, 3)):
+        assert s.advance() == 0
+    assert s.restore(ckpt) == 0
+    barrier(dist, torch)
+    L.qwen_b200_mark(2)
+    done = 0
+    while done < args.steps:
+        n = min(args.steps - done, window)
+        for _ in range(n):
+            assert s.advance() == 0
+        done += n
+        assert s.restore(ckpt) == 0
+    L.qwen_b200_mark(3)
+    L.gpu_sync()
+    e2e_ms = max_over_ranks(L.qwen_b200_elapsed_ms(2, 3), dist, torch)
+    barrier(dist, torch)
+
+    # Roofline of the dominant kernel: the fused gate/up GEMV (half the bytes).
+    es = 2 if cfg["profile"] == 2 else 4
+    gateup_ms = L.qwen_b200_time_stage(runner, 3, 0, pos0, 30)
+    gateup_bytes = 2 * shape.intermediate * shape.hidden * es + shape.intermediate * 4
+    peak, peak_kind = measured_peaks()
+    achieved = gateup_bytes / (gateup_ms * 1e-3) / 1e9
+    weight_bytes = model.weight_bytes
+    mean_ctx = pos0 + window / 2
+    kv_bytes = 2 * shape.layers * shape.kvheads * shape.head * 4 * mean_ctx
+    step_bytes = weight_bytes + kv_bytes
+    ms_per_step = device_ms / args.steps
+    stage_names = ["qkv", "attention", "oproj", "gateup", "down", "readout"]
+    stage_ms = {name: round(L.qwen_b200_time_stage(runner, i, 0, pos0, 10), 5) for i, name in enumerate(stage_names)}
+    s.free()
+    model.free()
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"gateup_{'bf16' if es == 2 else 'fp32'}")
+
+    line = {
+        "metric": METRIC, "value": round(args.steps * world / (device_ms * 1e-3), 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16-weights/f32" if es == 2 else "f32", "data": "synthetic",
+        "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": shape.layers, "batch": 1,
+                   "prompt_tokens": cfg["prompt"], "decode_window": window,
+                   "weights": "seeded N(0,0.02) random init", "parallelism": f"replicas{world}",
+                   "l2": "inputs larger than L2 (weights stream from HBM every step)"},
+        "e2e": {"value": round(args.steps * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 32},
+        "gpu_launches": per_token_launches * args.steps + (args.steps + window - 1) // window,
+        "roofline": {"bound": "hbm", "kernel": "gateup_kernel (RMSNorm + gate/up GEMV + SwiGLU)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": gateup_bytes,
+                     "launch_ms": round(gateup_ms, 5)},
+        "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
+                          "frac": round(step_bytes / (ms_per_step * 1e6) / peak, 4)},
+        "stage_ms_layer0": stage_ms,
+        "clocks": clocks.summary(),
+        "last_top2": top.tuple(),
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="fp32-ctx512")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
+        print(json.dumps({
+            "metric": METRIC, "impl": "reference", "value": round(rate, 4), "unit": "tokens/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16-weights/f32" if cfg["profile"] == 2 else "f32", "data": "synthetic",
+            "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": cfg["layers"], "batch": 1},
+            "cpu_baseline": {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(rate, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    world, rank, local, dist, torch = dist_setup(args.gpus)
+    line = run_b200(args, cfg, world, rank, local, dist, torch)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, sample, kind, ref_logits = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
+        line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
+                                "sample": sample}
+        line["max_abs_dlogit"] = gpu_dlogit(cfg["layers"], cfg["profile"], ref_logits)
+    if rank == 0:
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

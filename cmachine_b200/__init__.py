@@ -1,0 +1,282 @@
+"""Python mirror of the cmachine Qwen2.5 session API on the B200 library.
+
+The product is libcmachine_b200.so (C ABI: include/gpu.h, include/qwen.h,
+include/qwen_b200.h). This module loads it with ctypes and mirrors the
+reference's C entry points (src/qwen.h) one to one -- qwen_push,
+qwen_begin_token, qwen_advance_layer, qwen_finish_token, checkpoints, the
+nested stack, reset -- with the same return codes, so that tests and the
+benchmark drive exactly the calls a C host makes. There is no Python or CPU
+fallback: a missing library raises at import of `lib()`.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, Structure, c_float, c_int, c_size_t, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libcmachine_b200.so"
+
+
+class Shape(Structure):
+    """QwenB200Shape (include/qwen_b200.h)."""
+    _fields_ = [(n, c_int) for n in ("hidden", "layers", "qheads", "kvheads", "head", "intermediate", "vocab",
+                                     "max_position")] + [("epsilon", c_float), ("theta", c_float)]
+
+    def as_dict(self):
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class Fill(Structure):
+    _fields_ = [("offset", c_float), ("scale", c_float)]
+
+
+class FillLaw(Structure):
+    """TcmFillLaw (include/tcm_seeded.h)."""
+    _fields_ = [("matrix", Fill), ("norm", Fill), ("bias", Fill)]
+
+
+class Top2(Structure):
+    """TcmTop2 (include/gpu.h)."""
+    _fields_ = [("first", c_int), ("second", c_int), ("first_value", c_float), ("second_value", c_float)]
+
+    def tuple(self):
+        return (self.first, self.second, self.first_value, self.second_value)
+
+
+class SessionView(Structure):
+    _fields_ = [(n, c_int) for n in ("position", "capacity", "pending", "layer", "phase", "delivered",
+                                     "dense_layers", "fused")] + [
+        ("depth", ctypes.c_uint), ("session_id", c_uint64), ("epoch", c_uint64), ("lineage_id", c_uint64),
+        ("checkpoint_serial", c_uint64), ("top_frame", c_uint64), ("top", Top2), ("keys", c_void_p),
+        ("values", c_void_p), ("x", c_void_p), ("logits", c_void_p), ("allocated_bytes", c_size_t)]
+
+
+def qwen_shape(layers: int = 28, max_position: int = 32768) -> Shape:
+    """Qwen2.5-1.5B geometry (hidden 1536, 12/2 heads of 128, MLP 8960, vocab 151936)."""
+    return Shape(1536, layers, 12, 2, 128, 8960, 151936, max_position, 1e-6, 1e6)
+
+
+# Random-init laws: the benchmark's (linear/embedding N(0, 0.02), biases 0,
+# norms 1) and the parity tests' (nonzero biases, non-unit norms).
+BENCH_LAW = FillLaw(Fill(0.0, 0.02), Fill(1.0, 0.0), Fill(0.0, 0.0))
+TEST_LAW = FillLaw(Fill(0.0, 0.02), Fill(1.0, 0.1), Fill(0.0, 0.05))
+
+OBSERVER = ctypes.CFUNCTYPE(None, c_void_p, c_int, c_int, c_int, POINTER(c_float), c_size_t)
+PORT_NAMES = ["input", "query", "key", "value", "attention", "mlp_input", "mlp_gate", "mlp_up", "mlp_return",
+              "output", "attention_write", "raw_receiver", "consumed_attention_write", "consumed_mlp_write"]
+
+_LIB = None
+
+
+def _declare(L):
+    P = c_void_p
+    sig = {
+        # include/gpu.h
+        "gpu_open": (P, []), "gpu_close": (None, [P]), "gpu_alloc": (P, [c_size_t]), "gpu_free": (None, [P]),
+        "gpu_zero": (None, [P, c_size_t]), "gpu_copy": (None, [P, P, c_size_t]),
+        "gpu_read": (None, [P, P, c_size_t]), "gpu_write": (None, [P, P, c_size_t]), "gpu_sync": (None, []),
+        "gpu_live_bytes": (c_size_t, []), "gpu_peak_bytes": (c_size_t, []), "gpu_free_bytes": (c_size_t, []),
+        "gpu_weight": (P, [P, c_uint32, c_size_t]),
+        "gpu_matvec": (None, [P, P, c_int, c_int, P, P]),
+        "gpu_rms": (None, [P, P, P, c_int, c_float]), "gpu_rms_scale": (None, [P, P, P, c_int, c_float, P]),
+        "gpu_multiply": (None, [P, P, P, c_int]), "gpu_plane": (None, [P, P, P, P, c_int, c_float, c_float]),
+        "gpu_plane_scaled": (None, [P, P, P, P, c_int, c_float, c_float, P]),
+        "gpu_linear2": (None, [P, P, P, c_int, c_float, c_float, P]),
+        "gpu_identical_finite": (c_int, [P, P, P, c_int]), "gpu_add": (None, [P, P, c_int]),
+        "gpu_bias": (None, [P, P, c_int]), "gpu_rope": (None, [P, c_int, c_int, c_int, c_float]),
+        "gpu_cache": (None, [P, P, c_int, c_int, c_int, c_int]),
+        "gpu_attention": (None, [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int]),
+        "gpu_swiglu": (None, [P, P, c_int]), "gpu_gate_anchor": (None, [P, P, P, P, P, c_int]),
+        "gpu_gate_swiglu": (None, [P, P, P, P, P, P, P, c_int]), "gpu_top2": (Top2, [P, P, c_int]),
+        "gpu_weight_configure": (None, [c_int]),
+        "gpu_owned_weight": (P, [P, P, c_uint32, c_size_t, c_int, c_int, c_int]),
+        "gpu_owned_weight_bytes": (c_size_t, [P, c_size_t]), "gpu_owned_embedding": (None, [P, P, c_int, c_int]),
+        "gpu_weight_release": (None, []),
+        "gpu_weight_info": (None, [POINTER(c_size_t), POINTER(c_size_t), POINTER(c_size_t), POINTER(c_int),
+                                   POINTER(ctypes.c_ulonglong), POINTER(ctypes.c_ulonglong),
+                                   POINTER(ctypes.c_ulonglong)]),
+        "gpu_encode_current": (c_int, [P, P, P, P, P, c_int, c_int, P]),
+        "gpu_byte_attention": (None, [P, P, P, P, P, P, P, P, c_int, c_int]),
+        "gpu_ring_attention": (None, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int]),
+        # include/qwen.h
+        "qwen_model_init_seeded": (c_int, [P, POINTER(Shape), c_uint64, POINTER(FillLaw), c_int, c_int]),
+        "qwen_model_free": (None, [P]),
+        "qwen_session_init": (c_int, [P, P, c_int]),
+        "qwen_session_init_layout": (c_int, [P, P, c_int, c_uint64, P, P, P]),
+        "qwen_session_free": (None, [P]), "qwen_abort_token": (c_int, [P]), "qwen_push": (c_int, [P, c_int]),
+        "qwen_begin_token": (c_int, [P, c_int]), "qwen_advance_layer": (c_int, [P]),
+        "qwen_finish_token": (c_int, [P]), "qwen_advance": (c_int, [P]), "qwen_checkpoint": (c_int, [P, P]),
+        "qwen_restore": (c_int, [P, P]), "qwen_stack_push": (c_int, [P, POINTER(c_uint64)]),
+        "qwen_stack_rollback": (c_int, [P, c_uint64]), "qwen_stack_commit": (c_int, [P, c_uint64]),
+        "qwen_reset": (c_int, [P]), "qwen_port_name": (ctypes.c_char_p, [c_int]),
+        "qwen_generate": (c_int, [P, c_int, POINTER(c_int)]),
+        # include/qwen_b200.h
+        "qwen_b200_decoder_weight_bytes": (c_size_t, [P]),
+        "qwen_b200_launches_per_token": (c_int, [P]),
+        "qwen_b200_time_stage": (c_float, [P, c_int, c_int, c_int, c_int]),
+        "qwen_b200_enqueue": (c_int, [P, c_int, c_int, c_int]),
+        "qwen_b200_last": (c_int, [P, POINTER(Top2)]),
+        "qwen_b200_generate": (c_int, [P, c_int, c_int, c_int, POINTER(c_int), POINTER(Top2)]),
+        "qwen_b200_token": (c_int, [P, c_int, c_int, POINTER(Top2)]),
+        "qwen_b200_mark": (None, [c_int]), "qwen_b200_elapsed_ms": (c_float, [c_int, c_int]),
+        "qwen_b200_set_device": (None, [c_int]), "qwen_b200_sm_count": (c_int, []),
+        "qwen_b200_seeded_fill": (None, [P, c_int, c_uint64, c_uint32, c_size_t, c_float, c_float]),
+        # host/session_view.c
+        "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),
+        "qwen_b200_checkpoint_size": (c_size_t, []),
+        "qwen_b200_session_view": (None, [P, POINTER(SessionView)]),
+        "qwen_b200_session_set_delivered": (None, [P, c_int]),
+        "qwen_b200_session_observe": (None, [P, OBSERVER, P, c_int, c_int]),
+        "qwen_b200_model_weight_bytes": (c_size_t, [P]), "qwen_b200_model_decoder": (P, [P]),
+        "qwen_b200_session_runner": (P, [P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    return L
+
+
+def lib():
+    """The loaded library; raises if it was not built (no fallback path)."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m cmachine_b200.build`")
+        _LIB = _declare(ctypes.CDLL(str(LIB_PATH)))
+    return _LIB
+
+
+def ptr(a: np.ndarray):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class Model:
+    """A seeded random-init Qwen2.5-architecture model resident on the GPU."""
+
+    def __init__(self, shape: Shape, seed: int, law: FillLaw = BENCH_LAW, profile: int = 0, fused: bool = True):
+        L = lib()
+        self.shape, self.seed, self.law, self.profile = shape, seed, law, profile
+        self._buf = ctypes.create_string_buffer(L.qwen_b200_model_size())
+        self.handle = ctypes.cast(self._buf, c_void_p)
+        if L.qwen_model_init_seeded(self.handle, ctypes.byref(shape), seed, ctypes.byref(law), profile, int(fused)):
+            raise ValueError("qwen_model_init_seeded refused the shape")
+        self._live = True
+
+    @property
+    def weight_bytes(self) -> int:
+        return lib().qwen_b200_model_weight_bytes(self.handle)
+
+    def free(self):
+        if self._live:
+            lib().qwen_model_free(self.handle)
+            self._live = False
+
+
+class Checkpoint:
+    def __init__(self):
+        self._buf = ctypes.create_string_buffer(lib().qwen_b200_checkpoint_size())
+        self.handle = ctypes.cast(self._buf, c_void_p)
+
+
+class Session:
+    """A decode session; methods return the C entry point's status code."""
+
+    def __init__(self, model: Model, capacity: int):
+        L = lib()
+        self.model = model
+        self._buf = ctypes.create_string_buffer(L.qwen_b200_session_size())
+        self.handle = ctypes.cast(self._buf, c_void_p)
+        if L.qwen_session_init(self.handle, model.handle, capacity):
+            raise ValueError("qwen_session_init refused")
+        self._live = True
+        self._observer = None
+
+    # -- the reference's entry points (src/qwen.h:186-204)
+    def push(self, token: int) -> int: return lib().qwen_push(self.handle, token)
+    def begin_token(self, token: int) -> int: return lib().qwen_begin_token(self.handle, token)
+    def advance_layer(self) -> int: return lib().qwen_advance_layer(self.handle)
+    def finish_token(self) -> int: return lib().qwen_finish_token(self.handle)
+    def advance(self) -> int: return lib().qwen_advance(self.handle)
+    def abort_token(self) -> int: return lib().qwen_abort_token(self.handle)
+    def reset(self) -> int: return lib().qwen_reset(self.handle)
+
+    def checkpoint(self):
+        c = Checkpoint()
+        return lib().qwen_checkpoint(self.handle, c.handle), c
+
+    def restore(self, c: Checkpoint) -> int: return lib().qwen_restore(self.handle, c.handle)
+
+    def stack_push(self):
+        frame = c_uint64(0)
+        return lib().qwen_stack_push(self.handle, ctypes.byref(frame)), frame.value
+
+    def stack_rollback(self, frame: int) -> int: return lib().qwen_stack_rollback(self.handle, frame)
+    def stack_commit(self, frame: int) -> int: return lib().qwen_stack_commit(self.handle, frame)
+
+    def generate(self, n: int):
+        ids = (c_int * n)()
+        status = lib().qwen_generate(self.handle, n, ids)
+        return status, list(ids)
+
+    def set_delivered(self, delivered: int = 1): lib().qwen_b200_session_set_delivered(self.handle, delivered)
+
+    def observe(self, fn, position: int, layer: int):
+        """Arm the observer: fn(position, layer, port_name, np.ndarray copy)."""
+        L = lib()
+
+        def trampoline(_ctx, pos, lay, port, data, count):
+            host = np.empty(count, np.float32)
+            L.gpu_read(ptr(host), ctypes.cast(data, c_void_p), count * 4)
+            fn(pos, lay, PORT_NAMES[port], host)
+
+        self._observer = OBSERVER(trampoline)
+        L.qwen_b200_session_observe(self.handle, self._observer, None, position, layer)
+
+    # -- state readback
+    def view(self) -> SessionView:
+        v = SessionView()
+        lib().qwen_b200_session_view(self.handle, ctypes.byref(v))
+        return v
+
+    @property
+    def position(self) -> int: return self.view().position
+
+    @property
+    def pending(self) -> int: return self.view().pending
+
+    @property
+    def top(self): return self.view().top.tuple()
+
+    def logits(self) -> np.ndarray:
+        v = self.view()
+        out = np.empty(self.model.shape.vocab, np.float32)
+        lib().gpu_read(ptr(out), c_void_p(v.logits), out.nbytes)
+        return out
+
+    def hidden(self) -> np.ndarray:
+        v = self.view()
+        out = np.empty(self.model.shape.hidden, np.float32)
+        lib().gpu_read(ptr(out), c_void_p(v.x), out.nbytes)
+        return out
+
+    def kv(self, layer: int, kind: int) -> np.ndarray:
+        """K (kind 0) or V (kind 1) rows 0..position-1 of a dense layer: [kvheads][position][head]."""
+        v, s = self.view(), self.model.shape
+        out = np.empty((s.kvheads, v.position, s.head), np.float32)
+        base = (v.values if kind else v.keys) + layer * s.kvheads * v.capacity * s.head * 4
+        for h in range(s.kvheads):
+            if v.position:
+                lib().gpu_read(ptr(out[h]), c_void_p(base + h * v.capacity * s.head * 4), v.position * s.head * 4)
+        return out
+
+    @property
+    def runner(self): return lib().qwen_b200_session_runner(self.handle)
+
+    def free(self):
+        if self._live:
+            lib().qwen_session_free(self.handle)
+            self._live = False

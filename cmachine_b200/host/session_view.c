@@ -1,0 +1,43 @@
+/* Flat accessors over QwenModel / QwenSession for foreign-function callers
+ * (the Python mirror in cmachine_b200/__init__.py) that cannot lay out the C
+ * structs themselves. Pure field reads and writes; no arithmetic. */
+#include "../../include/qwen.h"
+#include <string.h>
+
+typedef struct {
+    int position, capacity, pending, layer, phase, delivered, dense_layers, fused;
+    unsigned depth;
+    uint64_t session_id, epoch, lineage_id, checkpoint_serial, top_frame;
+    TcmTop2 top;
+    float *keys, *values, *x, *logits;
+    size_t allocated_bytes;
+} QwenSessionView;
+
+size_t qwen_b200_model_size(void) { return sizeof(QwenModel); }
+size_t qwen_b200_session_size(void) { return sizeof(QwenSession); }
+size_t qwen_b200_checkpoint_size(void) { return sizeof(QwenCheckpoint); }
+
+void qwen_b200_session_view(const QwenSession *s, QwenSessionView *v) {
+    memset(v, 0, sizeof(*v));
+    v->position = s->position; v->capacity = s->capacity; v->pending = s->pending; v->layer = s->layer;
+    v->phase = s->phase; v->delivered = s->delivered; v->dense_layers = s->dense_layers; v->fused = s->runner != NULL;
+    v->depth = s->depth; v->session_id = s->session_id; v->epoch = s->epoch; v->lineage_id = s->lineage_id;
+    v->checkpoint_serial = s->checkpoint_serial; v->top_frame = s->depth ? s->frames[s->depth - 1].id : 0;
+    v->top = s->top; v->keys = s->keys; v->values = s->values; v->x = s->x; v->logits = s->logits;
+    v->allocated_bytes = s->allocated_bytes;
+}
+
+void qwen_b200_session_set_delivered(QwenSession *s, int delivered) { s->delivered = delivered; }
+
+void qwen_b200_session_observe(QwenSession *s, QwenObserver observer, void *context, int position, int layer) {
+    s->observer = observer;
+    s->observer_context = context;
+    s->observe_position = position;
+    s->observe_layer = layer;
+}
+
+void qwen_b200_session_cache_guard(QwenSession *s, QwenCacheGuard guard) { s->cache_guard = guard; }
+
+size_t qwen_b200_model_weight_bytes(const QwenModel *m) { return m->weight_bytes; }
+const QwenB200Decoder *qwen_b200_model_decoder(const QwenModel *m) { return m->fused; }
+QwenB200Runner *qwen_b200_session_runner(const QwenSession *s) { return s->runner; }

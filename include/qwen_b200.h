@@ -1,0 +1,121 @@
+/* Fused B200 decode entry points (additive to the reference ABI).
+ *
+ * The reference runs one decode token as ~24 primitive calls per layer and two
+ * blocking reads in gpu_top2 (src/qwen.c:216-387, src/qwen_cuda.cu:100-118).
+ * These entry points run the same equations as five fused sm_100a kernels per
+ * layer plus a fused vocabulary readout with greedy top-2, and replay a whole
+ * token as one CUDA graph:
+ *
+ *   layer: [RMSNorm -> q/k/v GEMV -> bias -> RoPE -> K/V append]
+ *          [split-K GQA attention]            (or the caller's cache step)
+ *          [O GEMV -> residual]
+ *          [RMSNorm -> gate/up GEMV -> SwiGLU]
+ *          [down GEMV -> residual]
+ *   token: [final RMSNorm -> tied-embedding GEMV -> logits + top-2 + finite check]
+ *
+ * They replace, in order, the reference's gpu_rms + qkv_apply + gpu_rope +
+ * gpu_cache (src/qwen.c:249-258), gpu_attention (src/qwen.c:259), gpu_matvec +
+ * gpu_add (src/qwen.c:262,275), gpu_rms + 2 gpu_matvec + gpu_swiglu
+ * (src/qwen.c:289,320,329), gpu_matvec + gpu_add (src/qwen.c:330,341), and
+ * gpu_rms + gpu_matvec + gpu_top2 (src/qwen.c:384). Weights and buffers are
+ * device pointers owned by the caller; weights are all FP32 or all BF16
+ * (source-BF16 residence); activations, K/V and accumulation are FP32.
+ * Errors: functions return 0, -1 for an invalid argument (nothing ran), or
+ * -3 when the logits held a non-finite value.
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#include "gpu.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int hidden, layers, qheads, kvheads, head, intermediate, vocab, max_position;
+    float epsilon, theta;
+} QwenB200Shape;
+
+/* One layer's tensors (device pointers), the reference's QwenLayer fields. */
+typedef struct {
+    const float *input_norm, *post_norm, *q, *k, *v, *qb, *kb, *vb, *o, *gate, *up, *down;
+} QwenB200Layer;
+
+/* A session's device buffers (the reference's QwenSession fields). keys and
+ * values are [dense layer][kvheads][capacity][head]; cache_slots[l] is the
+ * dense slot of layer l or -1 when a caller-supplied cache step owns it. */
+typedef struct {
+    float *keys, *values;
+    int capacity;
+    const int *cache_slots;
+    float *x, *q, *k, *v, *attention, *gate, *logits;
+} QwenB200Buffers;
+
+typedef struct QwenB200Decoder QwenB200Decoder;
+typedef struct QwenB200Runner QwenB200Runner;
+
+/* matrix_dtype: 1 FP32, 2 BF16, 0 = look the embedding up in the weight
+ * residence registry (gpu_owned_weight). Requires head == 128, qheads a
+ * multiple of kvheads with at most 8 query heads per KV head, hidden a multiple
+ * of 8. Returns NULL on an unsupported shape. */
+QwenB200Decoder *qwen_b200_decoder_create(const QwenB200Shape *shape, const float *embedding,
+                                          const float *final_norm, const QwenB200Layer *layers, int matrix_dtype);
+void qwen_b200_decoder_free(QwenB200Decoder *);
+/* HBM bytes one decode token streams for the weights (matrices + vectors). */
+size_t qwen_b200_decoder_weight_bytes(const QwenB200Decoder *);
+
+/* Per-session executor: scratch, device-resident token state, a CUDA graph of
+ * one whole token. Scratch comes from gpu_alloc (tracked). */
+QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *, const QwenB200Buffers *);
+void qwen_b200_runner_free(QwenB200Runner *);
+
+/* Token-level steps, for callers that drive layers one by one
+ * (qwen_begin_token / qwen_advance_layer / qwen_finish_token). */
+int qwen_b200_begin(QwenB200Runner *, int token, int position);
+int qwen_b200_layer(QwenB200Runner *, int layer);           /* all five stages (dense slot) */
+int qwen_b200_layer_qkv(QwenB200Runner *, int layer);       /* stage 1 (appends when dense) */
+int qwen_b200_layer_attention(QwenB200Runner *, int layer); /* stage 2 (dense slot) */
+int qwen_b200_layer_mlp(QwenB200Runner *, int layer);       /* stages 3-5 */
+int qwen_b200_finish(QwenB200Runner *, TcmTop2 *top);
+
+/* One whole token (embedding through top-2) as one graph replay; all layers
+ * must be dense. Same bits as begin + layers + finish. */
+int qwen_b200_token(QwenB200Runner *, int token, int position, TcmTop2 *top);
+/* n greedy tokens back to back: the device feeds each top-1 to the next step
+ * and advances the position; one host synchronisation at the end. ids[i] and
+ * tops[i] describe the readout after step i (ids may be NULL). */
+int qwen_b200_generate(QwenB200Runner *, int token, int position, int n, int *ids, TcmTop2 *tops);
+/* Enqueue n chained steps without waiting (timing and pipelining); the result
+ * of the last step is read by qwen_b200_last. */
+int qwen_b200_enqueue(QwenB200Runner *, int token, int position, int n);
+int qwen_b200_last(QwenB200Runner *, TcmTop2 *top);
+
+/* Kernel launches one token issues (for launch accounting). */
+int qwen_b200_launches_per_token(const QwenB200Runner *);
+/* Measurement aid: mean device time (ms, CUDA events) of one standalone launch
+ * of fused stage `stage` of `layer` (0 q/k/v, 1 attention, 2 O projection,
+ * 3 gate/up, 4 down, 5 readout) at `position`, over `reps` launches. */
+float qwen_b200_time_stage(QwenB200Runner *, int stage, int layer, int position, int reps);
+
+/* CUDA-event timing on the library stream: record marks 0..15, elapsed ms. */
+void qwen_b200_mark(int index);
+float qwen_b200_elapsed_ms(int from, int to);
+void qwen_b200_set_device(int device);
+int qwen_b200_sm_count(void);
+
+/* Register a device-resident matrix (rows x columns, FP32 or BF16 when
+ * encoded) with the weight residence registry, as gpu_owned_weight does for a
+ * host upload, so gpu_matvec reads it in its stored type. */
+void qwen_b200_register_matrix(const void *p, int rows, int columns, int encoded);
+void qwen_b200_unregister_matrix(const void *p);
+
+/* Seeded device fill (include/tcm_seeded.h): n values of tensor `id` under
+ * model seed `seed` with value offset + N(0,1)*scale, stored as FP32
+ * (dtype 1) or BF16 (dtype 2) at dst. */
+void qwen_b200_seeded_fill(void *dst, int dtype, uint64_t seed, uint32_t id, size_t n, float offset, float scale);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,45 @@
+/* Test infrastructure only: the C ABI shared by the two CPU checkers.
+ *
+ *   liboracle.so        -- this repository's C restatement of the reference's CPU
+ *                          FP32 decode path (qwen_oracle.c);
+ *   _ref/libref_cpu.so  -- the reference's own src/qwen.c + src/model.c +
+ *                          tests/gpu_stub.c, built from the reference sources by
+ *                          oracle/Makefile and driven through ref_driver.c.
+ *
+ * Both export the same orc_* symbols so tests can run them side by side. Nothing
+ * in the product links against these libraries.
+ */
+#ifndef TCM_ORACLE_API_H
+#define TCM_ORACLE_API_H
+#include <stdint.h>
+#include "../include/tcm_seeded.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+typedef struct {
+    int hidden, layers, qheads, kvheads, head, intermediate, vocab, max_position;
+    float epsilon, theta;
+} OrcShape;
+typedef struct { int first, second; float first_value, second_value; } OrcTop2;
+
+/* weights: 0 = FP32 values, 1 = matrices (and embedding) rounded to BF16 and
+ * consumed widened to FP32, as the reference's profile 0 / profile 2 do. */
+void *orc_model_create(const OrcShape *shape, uint64_t seed, const TcmFillLaw *law, int bf16);
+void orc_model_free(void *model);
+void *orc_session_create(void *model, int capacity);
+void orc_session_free(void *session);
+/* One qwen_push: returns 0 on success; writes top-2 and, if logits != NULL,
+ * all vocab logits of the readout that followed the token. The restatement
+ * (liboracle.so) skips the readout when top == NULL (cheap prefill). */
+int orc_push(void *session, int token, OrcTop2 *top, float *logits);
+int orc_position(void *session);
+/* K or V rows 0..position-1 of one layer: out[kvheads][position][head]. */
+void orc_read_kv(void *session, int layer, int kind, float *out);
+/* The final-norm input x of the last pushed token (hidden floats). */
+void orc_read_hidden(void *session, float *out);
+/* Seeded weight element readback for generator pinning: tensor id, index. */
+float orc_weight_value(void *model, uint32_t tensor, uint64_t index);
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,79 @@
+"""Test-side loaders for the CPU checkers under oracle/ (test infrastructure).
+
+liboracle.so is this repository's C restatement of the reference CPU path;
+_ref/libref_cpu.so is the reference's own CPU path built from its sources;
+_ref/libref_gpuhost.so is the reference's unchanged C host linked against
+libcmachine_b200.so. All three export the orc_* ABI of oracle/oracle_api.h.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+from cmachine_b200 import FillLaw, Shape, Top2
+
+ROOT = Path(__file__).resolve().parent.parent
+ORACLE = ROOT / "oracle" / "liboracle.so"
+REF_CPU = ROOT / "oracle" / "_ref" / "libref_cpu.so"
+REF_GPUHOST = ROOT / "oracle" / "_ref" / "libref_gpuhost.so"
+
+
+def load(path: Path):
+    if not path.exists():
+        raise FileNotFoundError(f"{path} missing: run __graft_entry__.build()")
+    L = ctypes.CDLL(str(path))
+    L.orc_model_create.restype = c_void_p
+    L.orc_model_create.argtypes = [POINTER(Shape), c_uint64, POINTER(FillLaw), c_int]
+    L.orc_model_free.argtypes = [c_void_p]
+    L.orc_session_create.restype = c_void_p
+    L.orc_session_create.argtypes = [c_void_p, c_int]
+    L.orc_session_free.argtypes = [c_void_p]
+    L.orc_push.argtypes = [c_void_p, c_int, c_void_p, c_void_p]
+    L.orc_position.argtypes = [c_void_p]
+    L.orc_read_kv.argtypes = [c_void_p, c_int, c_int, c_void_p]
+    L.orc_read_hidden.argtypes = [c_void_p, c_void_p]
+    L.orc_weight_value.restype = c_float
+    L.orc_weight_value.argtypes = [c_void_p, c_uint32, c_uint64]
+    return L
+
+
+class CpuDecoder:
+    """One CPU model + session of a checker library."""
+
+    def __init__(self, path: Path, shape: Shape, seed: int, law: FillLaw, bf16: bool, capacity: int):
+        self.L = load(path)
+        self.shape = shape
+        self.model = self.L.orc_model_create(ctypes.byref(shape), seed, ctypes.byref(law), int(bf16))
+        self.session = self.L.orc_session_create(self.model, capacity)
+        assert self.session, "checker refused the session"
+
+    def push(self, token: int, readout: bool = True, logits: bool = True):
+        if not readout:
+            assert self.L.orc_push(self.session, token, None, None) == 0
+            return None, None
+        top = Top2()
+        out = np.empty(self.shape.vocab, np.float32) if logits else None
+        assert self.L.orc_push(self.session, token, ctypes.byref(top),
+                               c_void_p(out.ctypes.data) if logits else None) == 0
+        return top.tuple(), out
+
+    def kv(self, layer: int, kind: int) -> np.ndarray:
+        pos = self.L.orc_position(self.session)
+        out = np.empty((self.shape.kvheads, pos, self.shape.head), np.float32)
+        self.L.orc_read_kv(self.session, layer, kind, c_void_p(out.ctypes.data))
+        return out
+
+    def hidden(self) -> np.ndarray:
+        out = np.empty(self.shape.hidden, np.float32)
+        self.L.orc_read_hidden(self.session, c_void_p(out.ctypes.data))
+        return out
+
+    def weight(self, tensor: int, index: int) -> float:
+        return self.L.orc_weight_value(self.model, tensor, index)
+
+    def close(self):
+        self.L.orc_session_free(self.session)
+        self.L.orc_model_free(self.model)
