@@ -71,7 +71,7 @@ PORT_NAMES = ["input", "query", "key", "value", "attention", "mlp_input", "mlp_g
 _LIB = None
 
 
-def _declare(L):
+def _declare(L, strict: bool = True):
     P = c_void_p
     sig = {
         # include/gpu.h
@@ -124,6 +124,8 @@ def _declare(L):
         "qwen_b200_mark": (None, [c_int]), "qwen_b200_elapsed_ms": (c_float, [c_int, c_int]),
         "qwen_b200_set_device": (None, [c_int]), "qwen_b200_sm_count": (c_int, []),
         "qwen_b200_seeded_fill": (None, [P, c_int, c_uint64, c_uint32, c_size_t, c_float, c_float]),
+        "qwen_b200_register_matrix": (None, [P, c_int, c_int, c_int]),
+        "qwen_b200_unregister_matrix": (None, [P]),
         # host/session_view.c
         "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),
         "qwen_b200_checkpoint_size": (c_size_t, []),
@@ -134,10 +136,21 @@ def _declare(L):
         "qwen_b200_session_runner": (P, [P]),
     }
     for name, (res, args) in sig.items():
-        fn = getattr(L, name)
+        try:
+            fn = getattr(L, name)
+        except AttributeError:
+            if strict:
+                raise
+            continue
         fn.restype = res
         fn.argtypes = args
     return L
+
+
+def load_library(path) -> ctypes.CDLL:
+    """Another build of the same C ABI (e.g. the session host linked against a
+    CPU primitive fake for host-logic tests); symbols it lacks stay undeclared."""
+    return _declare(ctypes.CDLL(str(path)), strict=False)
 
 
 def lib():
@@ -157,8 +170,9 @@ def ptr(a: np.ndarray):
 class Model:
     """A seeded random-init Qwen2.5-architecture model resident on the GPU."""
 
-    def __init__(self, shape: Shape, seed: int, law: FillLaw = BENCH_LAW, profile: int = 0, fused: bool = True):
-        L = lib()
+    def __init__(self, shape: Shape, seed: int, law: FillLaw = BENCH_LAW, profile: int = 0, fused: bool = True,
+                 library=None):
+        L = self.L = library or lib()
         self.shape, self.seed, self.law, self.profile = shape, seed, law, profile
         self._buf = ctypes.create_string_buffer(L.qwen_b200_model_size())
         self.handle = ctypes.cast(self._buf, c_void_p)
@@ -168,65 +182,68 @@ class Model:
 
     @property
     def weight_bytes(self) -> int:
-        return lib().qwen_b200_model_weight_bytes(self.handle)
+        return self.L.qwen_b200_model_weight_bytes(self.handle)
 
     def free(self):
         if self._live:
-            lib().qwen_model_free(self.handle)
+            self.L.qwen_model_free(self.handle)
             self._live = False
 
 
 class Checkpoint:
-    def __init__(self):
-        self._buf = ctypes.create_string_buffer(lib().qwen_b200_checkpoint_size())
+    def __init__(self, L=None):
+        L = L or lib()
+        self._buf = ctypes.create_string_buffer(L.qwen_b200_checkpoint_size())
         self.handle = ctypes.cast(self._buf, c_void_p)
 
 
 class Session:
     """A decode session; methods return the C entry point's status code."""
 
-    def __init__(self, model: Model, capacity: int):
-        L = lib()
+    def __init__(self, model: Model, capacity: int, mask: int = 0, step=None, rewind=None):
+        L = self.L = model.L
         self.model = model
         self._buf = ctypes.create_string_buffer(L.qwen_b200_session_size())
         self.handle = ctypes.cast(self._buf, c_void_p)
-        if L.qwen_session_init(self.handle, model.handle, capacity):
+        self._callbacks = (step, rewind)
+        as_ptr = lambda f: ctypes.cast(f, c_void_p) if f is not None else None
+        if L.qwen_session_init_layout(self.handle, model.handle, capacity, mask, as_ptr(step), as_ptr(rewind), None):
             raise ValueError("qwen_session_init refused")
         self._live = True
         self._observer = None
 
     # -- the reference's entry points (src/qwen.h:186-204)
-    def push(self, token: int) -> int: return lib().qwen_push(self.handle, token)
-    def begin_token(self, token: int) -> int: return lib().qwen_begin_token(self.handle, token)
-    def advance_layer(self) -> int: return lib().qwen_advance_layer(self.handle)
-    def finish_token(self) -> int: return lib().qwen_finish_token(self.handle)
-    def advance(self) -> int: return lib().qwen_advance(self.handle)
-    def abort_token(self) -> int: return lib().qwen_abort_token(self.handle)
-    def reset(self) -> int: return lib().qwen_reset(self.handle)
+    def push(self, token: int) -> int: return self.L.qwen_push(self.handle, token)
+    def begin_token(self, token: int) -> int: return self.L.qwen_begin_token(self.handle, token)
+    def advance_layer(self) -> int: return self.L.qwen_advance_layer(self.handle)
+    def finish_token(self) -> int: return self.L.qwen_finish_token(self.handle)
+    def advance(self) -> int: return self.L.qwen_advance(self.handle)
+    def abort_token(self) -> int: return self.L.qwen_abort_token(self.handle)
+    def reset(self) -> int: return self.L.qwen_reset(self.handle)
 
     def checkpoint(self):
-        c = Checkpoint()
-        return lib().qwen_checkpoint(self.handle, c.handle), c
+        c = Checkpoint(self.L)
+        return self.L.qwen_checkpoint(self.handle, c.handle), c
 
-    def restore(self, c: Checkpoint) -> int: return lib().qwen_restore(self.handle, c.handle)
+    def restore(self, c: Checkpoint) -> int: return self.L.qwen_restore(self.handle, c.handle)
 
     def stack_push(self):
         frame = c_uint64(0)
-        return lib().qwen_stack_push(self.handle, ctypes.byref(frame)), frame.value
+        return self.L.qwen_stack_push(self.handle, ctypes.byref(frame)), frame.value
 
-    def stack_rollback(self, frame: int) -> int: return lib().qwen_stack_rollback(self.handle, frame)
-    def stack_commit(self, frame: int) -> int: return lib().qwen_stack_commit(self.handle, frame)
+    def stack_rollback(self, frame: int) -> int: return self.L.qwen_stack_rollback(self.handle, frame)
+    def stack_commit(self, frame: int) -> int: return self.L.qwen_stack_commit(self.handle, frame)
 
     def generate(self, n: int):
         ids = (c_int * n)()
-        status = lib().qwen_generate(self.handle, n, ids)
+        status = self.L.qwen_generate(self.handle, n, ids)
         return status, list(ids)
 
-    def set_delivered(self, delivered: int = 1): lib().qwen_b200_session_set_delivered(self.handle, delivered)
+    def set_delivered(self, delivered: int = 1): self.L.qwen_b200_session_set_delivered(self.handle, delivered)
 
     def observe(self, fn, position: int, layer: int):
         """Arm the observer: fn(position, layer, port_name, np.ndarray copy)."""
-        L = lib()
+        L = self.L
 
         def trampoline(_ctx, pos, lay, port, data, count):
             host = np.empty(count, np.float32)
@@ -239,7 +256,7 @@ class Session:
     # -- state readback
     def view(self) -> SessionView:
         v = SessionView()
-        lib().qwen_b200_session_view(self.handle, ctypes.byref(v))
+        self.L.qwen_b200_session_view(self.handle, ctypes.byref(v))
         return v
 
     @property
@@ -254,13 +271,13 @@ class Session:
     def logits(self) -> np.ndarray:
         v = self.view()
         out = np.empty(self.model.shape.vocab, np.float32)
-        lib().gpu_read(ptr(out), c_void_p(v.logits), out.nbytes)
+        self.L.gpu_read(ptr(out), c_void_p(v.logits), out.nbytes)
         return out
 
     def hidden(self) -> np.ndarray:
         v = self.view()
         out = np.empty(self.model.shape.hidden, np.float32)
-        lib().gpu_read(ptr(out), c_void_p(v.x), out.nbytes)
+        self.L.gpu_read(ptr(out), c_void_p(v.x), out.nbytes)
         return out
 
     def kv(self, layer: int, kind: int) -> np.ndarray:
@@ -270,13 +287,13 @@ class Session:
         base = (v.values if kind else v.keys) + layer * s.kvheads * v.capacity * s.head * 4
         for h in range(s.kvheads):
             if v.position:
-                lib().gpu_read(ptr(out[h]), c_void_p(base + h * v.capacity * s.head * 4), v.position * s.head * 4)
+                self.L.gpu_read(ptr(out[h]), c_void_p(base + h * v.capacity * s.head * 4), v.position * s.head * 4)
         return out
 
     @property
-    def runner(self): return lib().qwen_b200_session_runner(self.handle)
+    def runner(self): return self.L.qwen_b200_session_runner(self.handle)
 
     def free(self):
         if self._live:
-            lib().qwen_session_free(self.handle)
+            self.L.qwen_session_free(self.handle)
             self._live = False

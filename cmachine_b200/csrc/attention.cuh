@@ -19,6 +19,8 @@ constexpr int kAttnTile = 32;      // cache rows per shared-memory tile
 constexpr int kAttnThreads = 256;  // 8 warps
 constexpr int kAttnMaxGroup = 8;   // query heads per KV head
 constexpr int kAttnSplits = 74;    // slices per KV head: 2 KV heads x 74 = 148 CTAs, one per SM
+constexpr int kAttnMinRows = 64;   // fewest cache rows per slice
+static_assert(kAttnSplits * kAttnMaxGroup <= 2 * kAttnTile * kHeadDim, "slice weights must fit a tile buffer");
 constexpr int kAttnPerThread = kAttnMaxGroup * kHeadDim / kAttnThreads;
 
 // Floats of one slice's partial result: m[8], l[8], acc[8][128].
@@ -94,13 +96,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     __shared__ float ks_s[2][kAttnTile], vs_s[2][kAttnTile];  // byte-codec row scales
     __shared__ int last_s;
 
-    const int kvh = blockIdx.y, split = blockIdx.x, nsplit = gridDim.x;
+    const int kvh = blockIdx.y, split = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvheads = gridDim.y;
     pdl_wait();
+    pdl_trigger();
+    // Slices of at least kAttnMinRows rows: short caches use few CTAs (cheap
+    // combine), long ones all of the grid. CTAs past the last slice leave.
     const int L = min(length >= 0 ? length : *position + 1, capacity);
-    const int chunk = (L + nsplit - 1) / nsplit;
-    const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
+    const int chunk = max((L + (int)gridDim.x - 1) / (int)gridDim.x, kAttnMinRows);
+    const int nsplit = (L + chunk - 1) / chunk;
+    if (split >= nsplit) return;
+    const int t0 = split * chunk, t1 = min(L, t0 + chunk);
     const float *kbase = nullptr, *vbase = nullptr, *ksc = nullptr, *vsc = nullptr;
     const int8_t *kcb = nullptr, *vcb = nullptr;
     if (BYTES) {
@@ -233,24 +240,36 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     __syncthreads();
     if (!last_s) return;
     __threadfence();
-    // Last CTA of this KV head: combine the slices in split order.
+    // Last CTA of this KV head: combine the slices in split order. Warp g finds
+    // head g's global max and per-slice weights exp(m_s - M); then every
+    // (head, dim) output sums its slices with independent loads.
     const float *all = part + (size_t)kvh * nsplit * kAttnPartialFloats;
+    float *w_s = k_tile;  // [kAttnMaxSplits][8] slice weights (tiles are free now)
+    if (warp < group) {
+        float M = -INFINITY;
+        for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(all + (size_t)s * kAttnPartialFloats + warp));
+        M = warp_max(M);
+        float den = 0.f;
+        for (int s = lane; s < nsplit; s += 32) {
+            const float *p = all + (size_t)s * kAttnPartialFloats;
+            const float m = __ldcg(p + warp);
+            const float w = m == -INFINITY ? 0.f : expf(m - M);
+            w_s[s * kAttnMaxGroup + warp] = w;
+            den = fmaf(w, __ldcg(p + kAttnMaxGroup + warp), den);
+        }
+        den = warp_sum(den);
+        if (lane == 0) c_s[warp] = den;
+    }
+    __syncthreads();
 #pragma unroll
     for (int j = 0; j < kAttnPerThread; j++) {
         const int g = j * (kAttnThreads / kHeadDim) + tid / kHeadDim, d = tid % kHeadDim;
         if (g >= group) continue;
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(all + (size_t)s * kAttnPartialFloats + g));
-        float num = 0.f, den = 0.f;
-        for (int s = 0; s < nsplit; s++) {
-            const float *p = all + (size_t)s * kAttnPartialFloats;
-            const float m = __ldcg(p + g);
-            if (m == -INFINITY) continue;
-            const float w = expf(m - M);
-            den = fmaf(w, __ldcg(p + kAttnMaxGroup + g), den);
-            num = fmaf(w, __ldcg(p + 2 * kAttnMaxGroup + g * kHeadDim + d), num);
-        }
-        out[((size_t)kvh * group + g) * kHeadDim + d] = __fdiv_rn(num, den);
+        const float *p = all + 2 * kAttnMaxGroup + g * kHeadDim + d;
+        float num = 0.f;
+#pragma unroll 8
+        for (int s = 0; s < nsplit; s++) num = fmaf(w_s[s * kAttnMaxGroup + g], __ldcg(p + (size_t)s * kAttnPartialFloats), num);
+        out[((size_t)kvh * group + g) * kHeadDim + d] = __fdiv_rn(num, c_s[g]);
     }
     if (tid == 0) counters[kvh] = 0u;
 }

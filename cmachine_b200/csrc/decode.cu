@@ -132,23 +132,50 @@ struct ResidualArgs {
     float *x;
     int in_dim, out_dim;
 };
-template <typename WT, int UNROLL>
+// KSPLIT warps share one row, each streaming a contiguous 1/KSPLIT of it; the
+// partial sums meet in shared memory and are added in split order.
+template <typename WT, int KSPLIT, int UNROLL>
 __global__ void __launch_bounds__(kBlock) residual_gemv_kernel(ResidualArgs a) {
     extern __shared__ __align__(16) float xs[];
-    const int lane = threadIdx.x & 31;
-    const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
+    __shared__ float part[kBlock / 32];
+    constexpr int kRowsPerCta = (kBlock / 32) / KSPLIT;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int local = warp / KSPLIT, piece = warp % KSPLIT;
     const WT *w = (const WT *)a.w;
-    if (gwarp < a.out_dim) prefetch_row_l2(w + (size_t)gwarp * a.in_dim, (size_t)a.in_dim * sizeof(WT), lane);
+    const int nvec = a.in_dim / WVec<WT>::kElems;
+    const int per = (nvec + KSPLIT - 1) / KSPLIT;
+    const int v0 = min(nvec, piece * per), v1 = min(nvec, v0 + per);
+    const size_t piece_bytes = (size_t)(v1 - v0) * 16;
+    {
+        const int row = blockIdx.x * kRowsPerCta + local;
+        if (row < a.out_dim)
+            prefetch_row_l2(w + (size_t)row * a.in_dim + (size_t)v0 * WVec<WT>::kElems, piece_bytes, lane);
+    }
     pdl_wait();
     pdl_trigger();
     for (int i = threadIdx.x; i < a.in_dim; i += blockDim.x) xs[i] = a.in[i];
     __syncthreads();
-    const int nvec = a.in_dim / WVec<WT>::kElems;
-    for (int row = gwarp; row < a.out_dim; row += nwarps) {
-        const WT *rows[1] = {w + (size_t)row * a.in_dim};
-        float acc[1];
-        warp_rows_dot<WT, 1, UNROLL>(rows, xs, nvec, lane, acc);
-        if (lane == 0) a.x[row] = __fadd_rn(a.x[row], acc[0]);
+    for (int base = blockIdx.x * kRowsPerCta; base < a.out_dim; base += gridDim.x * kRowsPerCta) {
+        const int row = base + local;
+        float acc[1] = {0.f};
+        if (row < a.out_dim) {
+            const WT *rows[1] = {w + (size_t)row * a.in_dim + (size_t)v0 * WVec<WT>::kElems};
+            warp_rows_partial<WT, 1, UNROLL>(rows, xs + (size_t)v0 * WVec<WT>::kElems, v1 - v0, lane, acc);
+            acc[0] = warp_sum(acc[0]);
+        }
+        if (KSPLIT == 1) {
+            if (lane == 0 && row < a.out_dim) a.x[row] = __fadd_rn(a.x[row], acc[0]);
+        } else {
+            if (lane == 0) part[warp] = acc[0];
+            __syncthreads();
+            if (piece == 0 && lane == 0 && row < a.out_dim) {
+                float sum = part[warp];
+#pragma unroll
+                for (int k = 1; k < KSPLIT; k++) sum = __fadd_rn(sum, part[warp + k]);
+                a.x[row] = __fadd_rn(a.x[row], sum);
+            }
+            __syncthreads();
+        }
     }
 }
 
@@ -289,8 +316,16 @@ template <typename T> inline void set_smem(T *kernel, int bytes) {
     TCM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 
-// GEMV unroll depths: 16-byte vectors in flight per row per lane.
-constexpr int kUnrollQkv = 6, kUnrollRes = 8, kUnrollGateUp = 6, kUnrollRead = 6;
+// GEMV shapes: 16-byte vectors in flight per row per lane (UNROLL) and warps
+// per row (KSPLIT). A 1536-wide FP32 row is 12 vectors per lane (one round of
+// loads); BF16 is 6. The 8960-wide down rows are split over 4 warps.
+template <typename WT> struct Tune;
+template <> struct Tune<float> {
+    static constexpr int kQkv = 12, kO = 12, kGateUp = 6, kRead = 12, kDownSplit = 4, kDown = 18;
+};
+template <> struct Tune<uint16_t> {
+    static constexpr int kQkv = 6, kO = 6, kGateUp = 6, kRead = 6, kDownSplit = 4, kDown = 9;
+};
 
 }  // namespace
 
@@ -338,10 +373,11 @@ struct QwenB200Runner {
 namespace {
 
 template <typename WT> void setup_kernels_typed() {
-    set_smem(qkv_kernel<WT, kUnrollQkv>, 64 * 1024);
-    set_smem(residual_gemv_kernel<WT, kUnrollRes>, 96 * 1024);
-    set_smem(gateup_kernel<WT, kUnrollGateUp>, 64 * 1024);
-    set_smem(readout_kernel<WT, kUnrollRead>, 64 * 1024);
+    set_smem(qkv_kernel<WT, Tune<WT>::kQkv>, 64 * 1024);
+    set_smem(residual_gemv_kernel<WT, 1, Tune<WT>::kO>, 96 * 1024);
+    set_smem(residual_gemv_kernel<WT, Tune<WT>::kDownSplit, Tune<WT>::kDown>, 96 * 1024);
+    set_smem(gateup_kernel<WT, Tune<WT>::kGateUp>, 64 * 1024);
+    set_smem(readout_kernel<WT, Tune<WT>::kRead>, 64 * 1024);
 }
 void setup_kernels() {
     static std::once_flag once;
@@ -372,7 +408,7 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.hidden = s.hidden; a.qheads = s.qheads; a.kvheads = s.kvheads; a.capacity = r->b.capacity; a.eps = s.epsilon;
     const int tasks = (s.qheads + 2 * s.kvheads) * 64;
     int grid = (tasks + kBlock / 32 - 1) / (kBlock / 32);
-    launch(qkv_kernel<WT, kUnrollQkv>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, a);
+    launch(qkv_kernel<WT, Tune<WT>::kQkv>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, a);
 }
 void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
@@ -387,7 +423,7 @@ template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl)
     const QwenB200Layer &L = r->d->layers[layer];
     ResidualArgs o = {L.o, r->b.attention, r->b.x, s.qheads * s.head, s.hidden};
     const int grid = (s.hidden + kBlock / 32 - 1) / (kBlock / 32);
-    launch(residual_gemv_kernel<WT, kUnrollRes>, dim3(grid), dim3(kBlock), (size_t)o.in_dim * 4, stream(), pdl, o);
+    launch(residual_gemv_kernel<WT, 1, Tune<WT>::kO>, dim3(grid), dim3(kBlock), (size_t)o.in_dim * 4, stream(), pdl, o);
 }
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
@@ -395,14 +431,16 @@ template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl
     GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, s.hidden, s.intermediate, s.epsilon};
     int grid = (s.intermediate + kBlock / 32 - 1) / (kBlock / 32);
     if (grid > r->grid_gemv) grid = r->grid_gemv;
-    launch(gateup_kernel<WT, kUnrollGateUp>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, g);
+    launch(gateup_kernel<WT, Tune<WT>::kGateUp>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, g);
 }
 template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
     const QwenB200Layer &L = r->d->layers[layer];
     ResidualArgs dn = {L.down, r->b.gate, r->b.x, s.intermediate, s.hidden};
-    const int grid = (s.hidden + kBlock / 32 - 1) / (kBlock / 32);
-    launch(residual_gemv_kernel<WT, kUnrollRes>, dim3(grid), dim3(kBlock), (size_t)dn.in_dim * 4, stream(), pdl, dn);
+    constexpr int split = Tune<WT>::kDownSplit, rows_per_cta = (kBlock / 32) / split;
+    const int grid = (s.hidden + rows_per_cta - 1) / rows_per_cta;
+    launch(residual_gemv_kernel<WT, split, Tune<WT>::kDown>, dim3(grid), dim3(kBlock), (size_t)dn.in_dim * 4, stream(),
+           pdl, dn);
 }
 template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl) {
     launch_oproj<WT>(r, layer, pdl);
@@ -416,7 +454,7 @@ template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
                      s.hidden, s.vocab, s.epsilon};
     int grid = (s.vocab + kBlock / 32 - 1) / (kBlock / 32);
     if (grid > r->grid_gemv) grid = r->grid_gemv;
-    launch(readout_kernel<WT, kUnrollRead>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, a);
+    launch(readout_kernel<WT, Tune<WT>::kRead>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, a);
 }
 
 void launch_layer(QwenB200Runner *r, int layer, bool pdl_first) {
