@@ -1,0 +1,35 @@
+"""A short decode run for profilers (ncu): builds a seeded Qwen2.5-architecture
+model, prefills a few tokens through qwen_push and generates a few more with
+qwen_generate, so that a launch list or a kernel capture sees the same kernels
+as a long decode without thousands of launches first.
+
+    python -m cmachine_b200.profile_decode --layers 28 --profile 0 --prompt 4 --tokens 2
+"""
+from __future__ import annotations
+
+import argparse
+
+import cmachine_b200 as cm
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--profile", type=int, choices=[0, 2], default=0, help="0 FP32 weights, 2 BF16 weights")
+    ap.add_argument("--prompt", type=int, default=4)
+    ap.add_argument("--tokens", type=int, default=2)
+    ap.add_argument("--seed", type=int, default=2026)
+    args = ap.parse_args()
+    model = cm.Model(cm.qwen_shape(args.layers, 32768), args.seed, cm.BENCH_LAW, args.profile)
+    session = cm.Session(model, args.prompt + args.tokens + 1)
+    for i in range(args.prompt):
+        assert session.push((i * 7919 + 11) % model.shape.vocab) == 0
+    status, ids = session.generate(args.tokens)
+    assert status == 0
+    print(f"prompt {args.prompt} tokens, generated {ids}")
+    session.free()
+    model.free()
+
+
+if __name__ == "__main__":
+    main()
