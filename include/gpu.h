@@ -74,6 +74,19 @@ void gpu_cache(float *cache, const float *x, int heads, int dim, int capacity, i
  * reads K/V head h / (qheads / kvheads); scores is scratch. (src/gpu.h:34) */
 void gpu_attention(TcmGpu *, float *out, const float *q, const float *keys, const float *values, float *scores,
                    int qheads, int kvheads, int dim, int capacity, int length);
+/* gpu_attention for callers that may not allocate device memory while they run
+ * (a host that owns all GPU memory through its own pool, a loop that cannot
+ * take cudaFree's device-wide synchronisation). No counterpart in the
+ * reference. Same result as gpu_attention for dim 128; no scores are written.
+ * Its split-K scratch is a fixed 1.2 MB device array inside the library, held
+ * by every GPU that loads it: limits are dim == 128, 1 <= kvheads <= 4, at most
+ * 8 query heads per KV head, 1 <= length <= capacity; other sizes return -1
+ * with a message on stderr and launch nothing. Returns 0 when launched. The
+ * first call on each device looks up the array's device address, so make it
+ * before any stream capture. Calls share the array: calls that overlap on the
+ * GPU race. */
+int gpu_attention_static(float *out, const float *q, const float *keys, const float *values, int qheads,
+                         int kvheads, int dim, int capacity, int length);
 /* gate = silu(gate) * up. (src/gpu.h:35) */
 void gpu_swiglu(float *gate, const float *up, int n);
 /* Experimental polynomial gate law. (src/gpu.h:36-38) */
