@@ -1,0 +1,179 @@
+// Decode attention for the fused path: split-K over the FP32 K/V cache with
+// every warp doing flash-decoding in registers.
+//
+// CTA (split, kv head) owns rows [t0, t1) (at least kAttnMinRows of them);
+// its four warps split those rows again. A lane holds 4 of the 128 head
+// dimensions: per step of four rows it loads the K and V rows (512-byte
+// coalesced reads, nothing staged in shared memory), forms the six query
+// heads' partial dots, reduces them across the warp, and updates each head's
+// running max, rescaled sum and accumulator. Warps then merge in a fixed order,
+// each CTA publishes (m, l, acc) per head, and the last CTA of the KV head
+// combines the slices in split order (deterministic). Scores are dot / sqrt(128)
+// as in the reference's CPU path (tests/gpu_stub.c:166).
+#pragma once
+#include "common.cuh"
+#include "attention.cuh"
+
+namespace tcm {
+
+constexpr int kDecodeAttnWarps = 4;
+constexpr int kDecodeAttnThreads = kDecodeAttnWarps * 32;
+
+template <int G>
+__global__ void __launch_bounds__(kDecodeAttnThreads) attn_decode_kernel(
+    const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
+    const int *__restrict__ position, float sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
+    float *__restrict__ out) {
+    __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
+    __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
+    __shared__ float slice_w[kAttnSplits][G];
+    __shared__ float den_s[G];
+    __shared__ int last_s;
+    const int kvh = blockIdx.y, split = blockIdx.x, kvheads = gridDim.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait();
+    pdl_trigger();
+    const int L = min(*position + 1, capacity);
+    const int chunk = max((L + (int)gridDim.x - 1) / (int)gridDim.x, kAttnMinRows);
+    const int nsplit = (L + chunk - 1) / chunk;
+    if (split >= nsplit) return;
+    const int t0 = split * chunk, t1 = min(L, t0 + chunk);
+    const int per_warp = (t1 - t0 + kDecodeAttnWarps - 1) / kDecodeAttnWarps;
+    const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
+    const float4 *kb = reinterpret_cast<const float4 *>(keys + (size_t)kvh * capacity * kHeadDim);
+    const float4 *vb = reinterpret_cast<const float4 *>(values + (size_t)kvh * capacity * kHeadDim);
+
+    float4 q4[G], acc[G];
+    float m[G], l[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        q4[g] = reinterpret_cast<const float4 *>(q + ((size_t)kvh * G + g) * kHeadDim)[lane];
+        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+    }
+    constexpr int kStep = 4;
+    for (int t = r0; t < r1; t += kStep) {
+        float4 k4[kStep], v4[kStep];
+#pragma unroll
+        for (int i = 0; i < kStep; i++) {
+            const bool ok = t + i < r1;
+            k4[i] = ok ? __ldcg(kb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v4[i] = ok ? __ldcg(vb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float s[kStep][G];
+#pragma unroll
+        for (int i = 0; i < kStep; i++)
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float d = q4[g].x * k4[i].x;
+                d = fmaf(q4[g].y, k4[i].y, d);
+                d = fmaf(q4[g].z, k4[i].z, d);
+                s[i][g] = fmaf(q4[g].w, k4[i].w, d);
+            }
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+#pragma unroll
+            for (int i = 0; i < kStep; i++)
+#pragma unroll
+                for (int g = 0; g < G; g++) s[i][g] += __shfl_xor_sync(0xffffffffu, s[i][g], o);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float mx = m[g];
+#pragma unroll
+            for (int i = 0; i < kStep; i++) {
+                s[i][g] = t + i < r1 ? __fdiv_rn(s[i][g], sqrt_dim) : -INFINITY;
+                mx = fmaxf(mx, s[i][g]);
+            }
+            const float c = m[g] == -INFINITY ? 0.f : expf(m[g] - mx);
+            float4 a = make_float4(acc[g].x * c, acc[g].y * c, acc[g].z * c, acc[g].w * c);
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < kStep; i++) {
+                const float p = s[i][g] == -INFINITY ? 0.f : expf(s[i][g] - mx);
+                sum += p;
+                a.x = fmaf(p, v4[i].x, a.x);
+                a.y = fmaf(p, v4[i].y, a.y);
+                a.z = fmaf(p, v4[i].z, a.z);
+                a.w = fmaf(p, v4[i].w, a.w);
+            }
+            acc[g] = a;
+            l[g] = fmaf(l[g], c, sum);
+            m[g] = mx;
+        }
+    }
+    // Merge the four warps (fixed order) into this CTA's slice result.
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        reinterpret_cast<float4 *>(wacc[warp][g])[lane] = acc[g];
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+    }
+    __syncthreads();
+    float *mine = part + ((size_t)kvh * nsplit + split) * kAttnPartialFloats;
+    {
+        const int d = tid;  // 128 threads, one head dimension each
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kDecodeAttnWarps; w++) M = fmaxf(M, wm[w][g]);
+            float num = 0.f, den = 0.f;
+#pragma unroll
+            for (int w = 0; w < kDecodeAttnWarps; w++) {
+                if (wm[w][g] == -INFINITY) continue;
+                const float e = expf(wm[w][g] - M);
+                den = fmaf(e, wl[w][g], den);
+                num = fmaf(e, wacc[w][g][d], num);
+            }
+            mine[2 * kAttnMaxGroup + g * kHeadDim + d] = num;
+            if (d == 0) {
+                mine[g] = M;
+                mine[kAttnMaxGroup + g] = den;
+            }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_s = atomicAdd(&counters[kvh], 1u) == (unsigned)(nsplit - 1);
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    // Last CTA of this KV head: weights exp(m_s - M) per slice, then every
+    // (head, dimension) sums its slices in split order.
+    const float *all = part + (size_t)kvh * nsplit * kAttnPartialFloats;
+    if (warp == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float M = -INFINITY;
+            for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(all + (size_t)s * kAttnPartialFloats + g));
+            M = warp_max(M);
+            float den = 0.f;
+            for (int s = lane; s < nsplit; s += 32) {
+                const float *p = all + (size_t)s * kAttnPartialFloats;
+                const float ms = __ldcg(p + g);
+                const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+                slice_w[s][g] = w;
+                den = fmaf(w, __ldcg(p + kAttnMaxGroup + g), den);
+            }
+            den = warp_sum(den);
+            if (lane == 0) den_s[g] = den;
+        }
+    }
+    __syncthreads();
+    const int d = tid;
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float *p = all + 2 * kAttnMaxGroup + g * kHeadDim + d;
+        float num = 0.f;
+#pragma unroll 8
+        for (int s = 0; s < nsplit; s++) num = fmaf(slice_w[s][g], __ldcg(p + (size_t)s * kAttnPartialFloats), num);
+        out[((size_t)kvh * G + g) * kHeadDim + d] = __fdiv_rn(num, den_s[g]);
+    }
+    if (tid == 0) counters[kvh] = 0u;
+    (void)kvheads;
+}
+
+}  // namespace tcm

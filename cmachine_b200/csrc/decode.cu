@@ -1,15 +1,19 @@
-// Fused batch-1 decode for the Qwen2.5 decoder on B200 (sm_100a).
+// Fused batch-1 decode for the Qwen2.5-1.5B decoder on B200 (sm_100a).
 //
-// Per layer five kernels, per token one readout kernel; all of them launched
-// with programmatic dependent launch so that each kernel's CTAs are resident
-// and prefetching their weight rows into L2 while the previous kernel drains,
-// and a whole token is captured once as a CUDA graph. Every kernel is a
-// warp-per-row GEMV streaming its weights from HBM exactly once (see gemv.cuh)
-// with the neighbouring elementwise work fused into its prologue/epilogue.
-// Reference equations: src/qwen.c:248-262,275,289,320,329-330,341,383-387.
+// Per layer five kernels, per token one readout kernel (reference equations:
+// src/qwen.c:248-262,275,289,320,329-330,341,383-387). Every GEMV kernel is a
+// persistent grid of one CTA per SM that owns a contiguous share of the rows
+// and streams them through a shared-memory ring with bulk copies (stream.cuh);
+// the input vector (RMS-normalised where the reference normalises) lives in
+// each consumer lane's registers. Kernels are launched with programmatic
+// dependent launch and trigger their dependents at once, so the next kernel's
+// CTAs become resident beside the running one and their producers fill the
+// first stages (up to ~100 KB per SM) before griddepcontrol.wait releases the
+// consumers. A whole token is captured once as a CUDA graph and replayed.
 #include "common.cuh"
-#include "gemv.cuh"
 #include "attention.cuh"
+#include "attention_decode.cuh"
+#include "stream.cuh"
 #include "kernels.h"
 #include "../../include/qwen_b200.h"
 #include "../../include/tcm_seeded.h"
@@ -20,197 +24,415 @@ namespace tcm {
 
 // Device-resident token state: the host writes token/position before a token;
 // the readout's last CTA publishes the top-2 and, for chained greedy decode,
-// feeds top-1 back as the next token and advances the position.
+// feeds top-1 back as the next token and advances the position. `fault`
+// collects the bits of any pipeline wait that ran out.
 struct DecodeState {
     int token, position, step, invalid;
+    unsigned fault;
+    int pad[3];
     TcmTop2 top;
 };
 constexpr int kLogCap = 4096;
 
 namespace {
 
-constexpr int kBlock = 256;
+constexpr int kHidden = 1536;       // Qwen2.5-1.5B hidden size (the fused kernels' geometry)
+constexpr int kInter = 8960;        // MLP width
+constexpr int kMaxPairsPerCta = 64; // q/k/v row pairs one CTA may own
 
-// ------------------------------------------------------------------ stage 1
+// Weight geometry: E elements per 16-byte vector; R rows of 1536 per stage
+// (48 KB either way); RD rows of 8960 per down stage (35 KB).
+template <typename WT> struct Geo;
+template <> struct Geo<float> { static constexpr int E = 4, R = 8, RD = 1; };
+template <> struct Geo<uint16_t> { static constexpr int E = 8, R = 16, RD = 2; };
+template <typename WT> constexpr int kNV = kHidden / (32 * Geo<WT>::E);  // vectors per lane in a row of 1536
+template <typename WT> constexpr uint32_t kRow = kHidden * sizeof(WT);
+template <typename WT> constexpr uint32_t kStage = Geo<WT>::R * kRow<WT>;
+template <typename WT> constexpr uint32_t kDownRow = kInter * sizeof(WT);
+template <typename WT> constexpr uint32_t kDownStage = Geo<WT>::RD * kDownRow<WT>;
+constexpr int kStages = 2, kDownStages = 3;
+constexpr int kLaneX = 48;  // floats of a 1536-vector one lane holds
+
+// ---------------------------------------------------------------- lane-resident vectors
+// Lane layout of a 1536-vector: lane owns 16-byte weight vectors v = lane + 32k
+// (k < kNV), i.e. elements E*v .. E*v+E-1, stored at xr[E*k ...].
+template <typename WT> __device__ __forceinline__ void load_lane_vec(float (&xr)[kLaneX], const float *x, int lane) {
+    constexpr int E = Geo<WT>::E;
+#pragma unroll
+    for (int k = 0; k < kNV<WT>; k++)
+#pragma unroll
+        for (int h = 0; h < E / 4; h++) {
+            const float4 f = reinterpret_cast<const float4 *>(x)[(E / 4) * (lane + 32 * k) + h];
+            xr[E * k + 4 * h] = f.x;
+            xr[E * k + 4 * h + 1] = f.y;
+            xr[E * k + 4 * h + 2] = f.z;
+            xr[E * k + 4 * h + 3] = f.w;
+        }
+}
+template <typename WT> __device__ __forceinline__ void store_lane_vec(float *x, const float (&xr)[kLaneX], int lane) {
+    constexpr int E = Geo<WT>::E;
+#pragma unroll
+    for (int k = 0; k < kNV<WT>; k++)
+#pragma unroll
+        for (int h = 0; h < E / 4; h++)
+            reinterpret_cast<float4 *>(x)[(E / 4) * (lane + 32 * k) + h] =
+                make_float4(xr[E * k + 4 * h], xr[E * k + 4 * h + 1], xr[E * k + 4 * h + 2], xr[E * k + 4 * h + 3]);
+}
+// A weight row (FP32 or BF16) of 1536 into the lane layout, widened to FP32.
+template <typename WT> __device__ __forceinline__ void load_lane_row(float (&xr)[kLaneX], const WT *row, int lane) {
+    if constexpr (sizeof(WT) == 4) {
+        load_lane_vec<float>(xr, reinterpret_cast<const float *>(row), lane);
+    } else {
+#pragma unroll
+        for (int k = 0; k < kNV<WT>; k++) {
+            const uint4 w = reinterpret_cast<const uint4 *>(row)[lane + 32 * k];
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                xr[8 * k + 2 * j] = bf16_lo(u[j]);
+                xr[8 * k + 2 * j + 1] = bf16_hi(u[j]);
+            }
+        }
+    }
+}
+// x <- (x * r) * w with r = 1 / sqrt(mean(x^2) + eps) over the whole warp's
+// vector; w is the norm weight vector staged in shared memory.
+template <typename WT> __device__ __forceinline__ void rms_lane(float (&xr)[kLaneX], const float *w_s, float eps, int lane) {
+    constexpr int E = Geo<WT>::E;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLaneX; i++) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHidden), eps)));
+#pragma unroll
+    for (int k = 0; k < kNV<WT>; k++)
+#pragma unroll
+        for (int j = 0; j < E; j++)
+            xr[E * k + j] = __fmul_rn(__fmul_rn(xr[E * k + j], r), w_s[E * (lane + 32 * k) + j]);
+}
+// The norm weights into shared memory (consumer threads; before the wait).
+__device__ __forceinline__ void stage_norm(float *w_s, const float *w) {
+    for (int i = threadIdx.x; i < kHidden / 4; i += kConsumerWarps * 32)
+        reinterpret_cast<float4 *>(w_s)[i] = reinterpret_cast<const float4 *>(w)[i];
+}
+__device__ __forceinline__ float dot_vec(const uint4 &w, const float *x, float acc, float) {
+    acc = fmaf(__uint_as_float(w.x), x[0], acc);
+    acc = fmaf(__uint_as_float(w.y), x[1], acc);
+    acc = fmaf(__uint_as_float(w.z), x[2], acc);
+    return fmaf(__uint_as_float(w.w), x[3], acc);
+}
+__device__ __forceinline__ float dot_vec(const uint4 &w, const float *x, float acc, uint16_t) {
+    acc = fmaf(bf16_lo(w.x), x[0], acc);
+    acc = fmaf(bf16_hi(w.x), x[1], acc);
+    acc = fmaf(bf16_lo(w.y), x[2], acc);
+    acc = fmaf(bf16_hi(w.y), x[3], acc);
+    acc = fmaf(bf16_lo(w.z), x[4], acc);
+    acc = fmaf(bf16_hi(w.z), x[5], acc);
+    acc = fmaf(bf16_lo(w.w), x[6], acc);
+    return fmaf(bf16_hi(w.w), x[7], acc);
+}
+// Warp dot product of a shared-memory row of 1536 with the lane-resident vector.
+template <typename WT> __device__ __forceinline__ float row_dot(const unsigned char *srow, const float (&xr)[kLaneX], int lane) {
+    const uint4 *v = reinterpret_cast<const uint4 *>(srow);
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNV<WT>; k++) acc = dot_vec(v[lane + 32 * k], &xr[Geo<WT>::E * k], acc, WT());
+    return warp_sum(acc);
+}
+__device__ __forceinline__ int share_begin(int total, int part, int parts) { return (int)((long long)part * total / parts); }
+
+// ---------------------------------------------------------------- stage 1: q/k/v
 struct QkvArgs {
     const void *wq, *wk, *wv, *embed;
     const float *bq, *bk, *bv, *norm, *rope_den;
     float *x, *q, *k, *v, *kcache, *vcache;
-    const DecodeState *st;
-    int hidden, qheads, kvheads, capacity;
+    DecodeState *st;
+    int qheads, kvheads, capacity;
     float eps;
 };
-
-// Task t = (head, d), head over q | k | v heads, d < 64: the warp computes rows
-// d and d + 64 of that head, adds the bias, rotates the pair (RoPE, q and k
-// only) and stores q, or k/v plus the cache row at the current position.
-template <typename WT, int UNROLL>
-__global__ void __launch_bounds__(kBlock) qkv_kernel(QkvArgs a) {
-    extern __shared__ __align__(16) float xs[];
-    __shared__ float red[32];
-    const int lane = threadIdx.x & 31;
-    const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
-    const int tasks = (a.qheads + 2 * a.kvheads) * 64;
-    const int nvec = a.hidden / WVec<WT>::kElems;
-    auto rows_of = [&](int task, const WT *(&rows)[2], const float *&bias, int &kind, int &hl, int &r0) {
-        const int head = task >> 6, d = task & 63;
+// Items are q/k/v rows in RoPE pairs: pair p = (head, d < 64) is rows d and
+// d + 64 of that head. Each stage holds R rows = R/2 pairs; the epilogue adds
+// the bias, rotates (q and k), stores q / k / v and appends k, v to the cache.
+template <typename WT>
+__global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int R = Geo<WT>::R;
+    __shared__ float res[2][R];
+    __shared__ float bias_s[2 * kMaxPairsPerCta];
+    __shared__ float den_s[kHeadDim / 2];
+    __shared__ __align__(16) float nw_s[kHidden];
+    __shared__ int fail_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pairs = (a.qheads + 2 * a.kvheads) * 64;
+    const int p0 = share_begin(pairs, blockIdx.x, gridDim.x), p1 = share_begin(pairs, blockIdx.x + 1, gridDim.x);
+    const int items = 2 * (p1 - p0);
+    auto locate = [&](int i, int &kind, int &hl, int &d) -> const WT * {
+        const int p = p0 + (i >> 1), head = p >> 6;
+        d = (p & 63) + 64 * (i & 1);
         const WT *base;
-        if (head < a.qheads) { base = (const WT *)a.wq; bias = a.bq; kind = 0; hl = head; }
-        else if (head < a.qheads + a.kvheads) { base = (const WT *)a.wk; bias = a.bk; kind = 1; hl = head - a.qheads; }
-        else { base = (const WT *)a.wv; bias = a.bv; kind = 2; hl = head - a.qheads - a.kvheads; }
-        r0 = hl * kHeadDim + d;
-        rows[0] = base + (size_t)r0 * a.hidden;
-        rows[1] = base + (size_t)(r0 + 64) * a.hidden;
+        if (head < a.qheads) { kind = 0; hl = head; base = (const WT *)a.wq; }
+        else if (head < a.qheads + a.kvheads) { kind = 1; hl = head - a.qheads; base = (const WT *)a.wk; }
+        else { kind = 2; hl = head - a.qheads - a.kvheads; base = (const WT *)a.wv; }
+        return base + (size_t)(hl * kHeadDim + d) * kHidden;
     };
-    if (gwarp < tasks) {
-        const WT *rows[2]; const float *bias; int kind, hl, r0;
-        rows_of(gwarp, rows, bias, kind, hl, r0);
-        prefetch_row_l2(rows[0], (size_t)a.hidden * sizeof(WT), lane);
-        prefetch_row_l2(rows[1], (size_t)a.hidden * sizeof(WT), lane);
-    }
-    pdl_wait();
+    if (threadIdx.x == 0) fail_s = 0;
+    const Ring ring = ring_setup(smem, kStages, kStage<WT>);
     pdl_trigger();
-    const int pos = a.st->position;
-    // Stage the layer input (the token's embedding row for layer 0) and its RMS norm.
-    float ss = 0.f;
-    if (a.embed) {
-        const size_t off = (size_t)a.st->token * a.hidden;
-        for (int i = threadIdx.x; i < a.hidden; i += blockDim.x) {
-            float v;
-            if constexpr (sizeof(WT) == 4) v = ((const float *)a.embed)[off + i];
-            else v = __uint_as_float((uint32_t)((const uint16_t *)a.embed)[off + i] << 16);
-            xs[i] = v;
-            if (blockIdx.x == 0) a.x[i] = v;
-            ss = fmaf(v, v, ss);
-        }
-    } else {
-        for (int i = threadIdx.x; i < a.hidden; i += blockDim.x) {
-            const float v = a.x[i];
-            xs[i] = v;
-            ss = fmaf(v, v, ss);
-        }
+    if (warp == kConsumerWarps) {
+        if (lane == 0)
+            ring_produce(ring, items, R, kRow<WT>, [&](int i) { int kd, hl, d; return (const void *)locate(i, kd, hl, d); },
+                         &a.st->fault);
+        return;
     }
-    const float total = block_sum(ss, red);
-    const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)a.hidden), a.eps)));
-    for (int i = threadIdx.x; i < a.hidden; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), a.norm[i]);
-    __syncthreads();
-    for (int task = gwarp; task < tasks; task += nwarps) {
-        const WT *rows[2]; const float *bias; int kind, hl, r0;
-        rows_of(task, rows, bias, kind, hl, r0);
-        float acc[2];
-        warp_rows_dot<WT, 2, UNROLL>(rows, xs, nvec, lane, acc);
-        if (lane == 0) {
-            float y0 = __fadd_rn(acc[0], bias[r0]), y1 = __fadd_rn(acc[1], bias[r0 + 64]);
+    // Constants first (they do not depend on earlier kernels).
+    stage_norm(nw_s, a.norm);
+    for (int i = threadIdx.x; i < items; i += kConsumerWarps * 32) {
+        int kind, hl, d;
+        locate(i, kind, hl, d);
+        const float *b = kind == 0 ? a.bq : kind == 1 ? a.bk : a.bv;
+        bias_s[i] = b[hl * kHeadDim + d];
+    }
+    if (threadIdx.x < kHeadDim / 2) den_s[threadIdx.x] = a.rope_den[threadIdx.x];
+    pdl_wait();
+    const int pos = a.st->position;
+    float xr[kLaneX];
+    if (a.embed) {
+        load_lane_row<WT>(xr, (const WT *)a.embed + (size_t)a.st->token * kHidden, lane);
+        if (blockIdx.x == 0 && warp == 0) store_lane_vec<WT>(a.x, xr, lane);
+    } else {
+        load_lane_vec<WT>(xr, a.x, lane);
+    }
+    consumers_sync();
+    rms_lane<WT>(xr, nw_s, a.eps, lane);
+    const int groups = (items + R - 1) / R;
+    for (int g = 0; g < groups; g++) {
+        const int n = min(R, items - g * R);
+        if (ring_acquire(ring, g, &a.st->fault)) {
+            const unsigned char *stage = ring.stage(g % kStages);
+#pragma unroll
+            for (int m = 0; m < R / kConsumerWarps; m++) {
+                const int j = warp + kConsumerWarps * m;
+                if (j < n) {
+                    const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
+                    if (lane == 0) res[g & 1][j] = y;
+                }
+            }
+        } else {
+            fail_s = 1;
+        }
+        ring_release(ring, g);
+        consumers_sync();
+        if (fail_s) break;
+        if ((int)threadIdx.x < n / 2) {
+            const int t = threadIdx.x, i = g * R + 2 * t;
+            int kind, hl, d;
+            locate(i, kind, hl, d);
+            float y0 = __fadd_rn(res[g & 1][2 * t], bias_s[i]), y1 = __fadd_rn(res[g & 1][2 * t + 1], bias_s[i + 1]);
             if (kind < 2) {
-                const float angle = __fdiv_rn((float)pos, a.rope_den[task & 63]);
+                const float angle = __fdiv_rn((float)pos, den_s[d]);
                 float sn, cs;
                 sincosf(angle, &sn, &cs);
-                const float t0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
-                const float t1 = __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn));
-                y0 = t0;
-                y1 = t1;
+                const float r0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+                const float r1 = __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn));
+                y0 = r0;
+                y1 = r1;
             }
             float *dst = kind == 0 ? a.q : kind == 1 ? a.k : a.v;
-            dst[r0] = y0;
-            dst[r0 + 64] = y1;
+            dst[hl * kHeadDim + d] = y0;
+            dst[hl * kHeadDim + d + 64] = y1;
             float *cache = kind == 1 ? a.kcache : kind == 2 ? a.vcache : nullptr;
             if (cache && pos >= 0 && pos < a.capacity) {
                 float *row = cache + ((size_t)hl * a.capacity + pos) * kHeadDim;
-                row[task & 63] = y0;
-                row[(task & 63) + 64] = y1;
+                row[d] = y0;
+                row[d + 64] = y1;
             }
         }
     }
 }
 
-// ------------------------------------------------------------------ stages 3 and 5
-// x[row] += W[row] . in  (O projection over the attention output, and the down
-// projection over the SwiGLU output).
-struct ResidualArgs {
+// ---------------------------------------------------------------- stage 3: O projection + residual
+struct ORowsArgs {
     const void *w;
     const float *in;
     float *x;
-    int in_dim, out_dim;
+    DecodeState *st;
 };
-// KSPLIT warps share one row, each streaming a contiguous 1/KSPLIT of it; the
-// partial sums meet in shared memory and are added in split order.
-template <typename WT, int KSPLIT, int UNROLL>
-__global__ void __launch_bounds__(kBlock) residual_gemv_kernel(ResidualArgs a) {
-    extern __shared__ __align__(16) float xs[];
-    __shared__ float part[kBlock / 32];
-    constexpr int kRowsPerCta = (kBlock / 32) / KSPLIT;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int local = warp / KSPLIT, piece = warp % KSPLIT;
+template <typename WT>
+__global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int R = Geo<WT>::R;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = share_begin(kHidden, blockIdx.x, gridDim.x), r1 = share_begin(kHidden, blockIdx.x + 1, gridDim.x);
+    const int items = r1 - r0;
     const WT *w = (const WT *)a.w;
-    const int nvec = a.in_dim / WVec<WT>::kElems;
-    const int per = (nvec + KSPLIT - 1) / KSPLIT;
-    const int v0 = min(nvec, piece * per), v1 = min(nvec, v0 + per);
-    const size_t piece_bytes = (size_t)(v1 - v0) * 16;
-    {
-        const int row = blockIdx.x * kRowsPerCta + local;
-        if (row < a.out_dim)
-            prefetch_row_l2(w + (size_t)row * a.in_dim + (size_t)v0 * WVec<WT>::kElems, piece_bytes, lane);
+    const Ring ring = ring_setup(smem, kStages, kStage<WT>);
+    pdl_trigger();
+    if (warp == kConsumerWarps) {
+        if (lane == 0)
+            ring_produce(ring, items, R, kRow<WT>, [&](int i) { return (const void *)(w + (size_t)(r0 + i) * kHidden); },
+                         &a.st->fault);
+        return;
     }
     pdl_wait();
-    pdl_trigger();
-    for (int i = threadIdx.x; i < a.in_dim; i += blockDim.x) xs[i] = a.in[i];
-    __syncthreads();
-    for (int base = blockIdx.x * kRowsPerCta; base < a.out_dim; base += gridDim.x * kRowsPerCta) {
-        const int row = base + local;
-        float acc[1] = {0.f};
-        if (row < a.out_dim) {
-            const WT *rows[1] = {w + (size_t)row * a.in_dim + (size_t)v0 * WVec<WT>::kElems};
-            warp_rows_partial<WT, 1, UNROLL>(rows, xs + (size_t)v0 * WVec<WT>::kElems, v1 - v0, lane, acc);
-            acc[0] = warp_sum(acc[0]);
-        }
-        if (KSPLIT == 1) {
-            if (lane == 0 && row < a.out_dim) a.x[row] = __fadd_rn(a.x[row], acc[0]);
-        } else {
-            if (lane == 0) part[warp] = acc[0];
-            __syncthreads();
-            if (piece == 0 && lane == 0 && row < a.out_dim) {
-                float sum = part[warp];
+    float xr[kLaneX];
+    load_lane_vec<WT>(xr, a.in, lane);
+    const int groups = (items + R - 1) / R;
+    for (int g = 0; g < groups; g++) {
+        if (!ring_acquire(ring, g, &a.st->fault)) break;
+        const int n = min(R, items - g * R);
+        const unsigned char *stage = ring.stage(g % kStages);
 #pragma unroll
-                for (int k = 1; k < KSPLIT; k++) sum = __fadd_rn(sum, part[warp + k]);
-                a.x[row] = __fadd_rn(a.x[row], sum);
+        for (int m = 0; m < R / kConsumerWarps; m++) {
+            const int j = warp + kConsumerWarps * m;
+            if (j < n) {
+                const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
+                if (lane == 0) a.x[r0 + g * R + j] = __fadd_rn(a.x[r0 + g * R + j], y);
             }
-            __syncthreads();
         }
+        ring_release(ring, g);
     }
 }
 
-// ------------------------------------------------------------------ stage 4
+// ---------------------------------------------------------------- stage 4: gate/up + SwiGLU
 struct GateUpArgs {
     const void *wg, *wu;
     const float *norm, *x;
     float *h;
-    int hidden, inter;
+    DecodeState *st;
     float eps;
 };
-template <typename WT, int UNROLL>
-__global__ void __launch_bounds__(kBlock) gateup_kernel(GateUpArgs a) {
-    extern __shared__ __align__(16) float xs[];
-    __shared__ float red[32];
-    const int lane = threadIdx.x & 31;
-    const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
+// Items alternate gate row j, up row j; the epilogue forms h_j = silu(g) * u
+// as g / (1 + exp(-g)) * u (src/qwen_cuda.cu:79).
+template <typename WT>
+__global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int R = Geo<WT>::R;
+    __shared__ float res[2][R];
+    __shared__ __align__(16) float nw_s[kHidden];
+    __shared__ int fail_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j0 = share_begin(kInter, blockIdx.x, gridDim.x), j1 = share_begin(kInter, blockIdx.x + 1, gridDim.x);
+    const int items = 2 * (j1 - j0);
     const WT *wg = (const WT *)a.wg, *wu = (const WT *)a.wu;
-    if (gwarp < a.inter) {
-        prefetch_row_l2(wg + (size_t)gwarp * a.hidden, (size_t)a.hidden * sizeof(WT), lane);
-        prefetch_row_l2(wu + (size_t)gwarp * a.hidden, (size_t)a.hidden * sizeof(WT), lane);
-    }
-    pdl_wait();
+    if (threadIdx.x == 0) fail_s = 0;
+    const Ring ring = ring_setup(smem, kStages, kStage<WT>);
     pdl_trigger();
-    stage_rms(xs, a.x, a.norm, a.hidden, a.eps, red);
-    const int nvec = a.hidden / WVec<WT>::kElems;
-    for (int j = gwarp; j < a.inter; j += nwarps) {
-        const WT *rows[2] = {wg + (size_t)j * a.hidden, wu + (size_t)j * a.hidden};
-        float acc[2];
-        warp_rows_dot<WT, 2, UNROLL>(rows, xs, nvec, lane, acc);
-        if (lane == 0) a.h[j] = __fmul_rn(__fdiv_rn(acc[0], __fadd_rn(1.f, expf(-acc[0]))), acc[1]);
+    if (warp == kConsumerWarps) {
+        if (lane == 0)
+            ring_produce(ring, items, R, kRow<WT>,
+                         [&](int i) { return (const void *)((i & 1 ? wu : wg) + (size_t)(j0 + (i >> 1)) * kHidden); },
+                         &a.st->fault);
+        return;
+    }
+    stage_norm(nw_s, a.norm);
+    pdl_wait();
+    float xr[kLaneX];
+    load_lane_vec<WT>(xr, a.x, lane);
+    consumers_sync();
+    rms_lane<WT>(xr, nw_s, a.eps, lane);
+    const int groups = (items + R - 1) / R;
+    for (int g = 0; g < groups; g++) {
+        const int n = min(R, items - g * R);
+        if (ring_acquire(ring, g, &a.st->fault)) {
+            const unsigned char *stage = ring.stage(g % kStages);
+#pragma unroll
+            for (int m = 0; m < R / kConsumerWarps; m++) {
+                const int j = warp + kConsumerWarps * m;
+                if (j < n) {
+                    const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
+                    if (lane == 0) res[g & 1][j] = y;
+                }
+            }
+        } else {
+            fail_s = 1;
+        }
+        ring_release(ring, g);
+        consumers_sync();
+        if (fail_s) break;
+        if ((int)threadIdx.x < n / 2) {
+            const int t = threadIdx.x;
+            const float gv = res[g & 1][2 * t], uv = res[g & 1][2 * t + 1];
+            a.h[j0 + (g * R) / 2 + t] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv);
+        }
     }
 }
 
-// ------------------------------------------------------------------ readout
+// ---------------------------------------------------------------- stage 5: down projection + residual
+struct DownArgs {
+    const void *w;
+    const float *h;
+    float *x;
+    DecodeState *st;
+};
+// A stage holds RD rows of 8960; 8 / RD warps split each row into contiguous
+// pieces of 280 vectors; the pieces are summed in order into the residual.
+template <typename WT>
+__global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int RD = Geo<WT>::RD, E = Geo<WT>::E, PIECES = kConsumerWarps / RD;
+    constexpr int NVP = kInter / E / PIECES;  // vectors per piece (280)
+    constexpr int KV = (NVP + 31) / 32;       // per lane (9)
+    __shared__ float part_s[2][RD][PIECES];
+    __shared__ int fail_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = warp / PIECES, piece = warp % PIECES;
+    const int r0 = share_begin(kHidden, blockIdx.x, gridDim.x), r1 = share_begin(kHidden, blockIdx.x + 1, gridDim.x);
+    const int items = r1 - r0;
+    const WT *w = (const WT *)a.w;
+    if (threadIdx.x == 0) fail_s = 0;
+    const Ring ring = ring_setup(smem, kDownStages, kDownStage<WT>);
+    pdl_trigger();
+    if (warp == kConsumerWarps) {
+        if (lane == 0)
+            ring_produce(ring, items, RD, kDownRow<WT>, [&](int i) { return (const void *)(w + (size_t)(r0 + i) * kInter); },
+                         &a.st->fault);
+        return;
+    }
+    pdl_wait();
+    float hr[KV * E];
+#pragma unroll
+    for (int k = 0; k < KV; k++) {
+        const int v = piece * NVP + lane + 32 * k;
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (lane + 32 * k < NVP) f = reinterpret_cast<const float4 *>(a.h)[(E * v + e) / 4];
+            hr[E * k + e] = f.x;
+            hr[E * k + e + 1] = f.y;
+            hr[E * k + e + 2] = f.z;
+            hr[E * k + e + 3] = f.w;
+        }
+    }
+    const int groups = (items + RD - 1) / RD;
+    for (int g = 0; g < groups; g++) {
+        const int n = min(RD, items - g * RD);
+        if (ring_acquire(ring, g, &a.st->fault)) {
+            if (slot < n) {
+                const uint4 *row = reinterpret_cast<const uint4 *>(ring.stage(g % kDownStages) + (size_t)slot * kDownRow<WT>);
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < KV; k++)
+                    if (lane + 32 * k < NVP) acc = dot_vec(row[piece * NVP + lane + 32 * k], &hr[E * k], acc, WT());
+                acc = warp_sum(acc);
+                if (lane == 0) part_s[g & 1][slot][piece] = acc;
+            }
+        } else {
+            fail_s = 1;
+        }
+        ring_release(ring, g);
+        consumers_sync();
+        if (fail_s) break;
+        if ((int)threadIdx.x < n) {
+            const int s = threadIdx.x, row = r0 + g * RD + s;
+            float sum = part_s[g & 1][s][0];
+#pragma unroll
+            for (int p = 1; p < PIECES; p++) sum = __fadd_rn(sum, part_s[g & 1][s][p]);
+            a.x[row] = __fadd_rn(a.x[row], sum);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- readout + greedy top-2
 struct ReadoutArgs {
     const void *embed;
     const float *norm, *x;
@@ -220,43 +442,65 @@ struct ReadoutArgs {
     unsigned *sync;  // [0] block counter, [1] non-finite flag
     DecodeState *st;
     TcmTop2 *log;
-    int hidden, vocab;
+    int vocab;
     float eps;
 };
-template <typename WT, int UNROLL>
-__global__ void __launch_bounds__(kBlock) readout_kernel(ReadoutArgs a) {
-    extern __shared__ __align__(16) float xs[];
-    __shared__ float red[32];
-    __shared__ float sv[2 * 32];
-    __shared__ int si[2 * 32];
+template <typename WT>
+__global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int R = Geo<WT>::R;
+    __shared__ float sv[2 * kConsumerWarps];
+    __shared__ int si[2 * kConsumerWarps];
+    __shared__ __align__(16) float nw_s[kHidden];
     __shared__ int last;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = share_begin(a.vocab, blockIdx.x, gridDim.x), r1 = share_begin(a.vocab, blockIdx.x + 1, gridDim.x);
+    const int items = r1 - r0;
     const WT *e = (const WT *)a.embed;
-    if (gwarp < a.vocab) prefetch_row_l2(e + (size_t)gwarp * a.hidden, (size_t)a.hidden * sizeof(WT), lane);
-    pdl_wait();
+    const Ring ring = ring_setup(smem, kStages, kStage<WT>);
     pdl_trigger();
-    stage_rms(xs, a.x, a.norm, a.hidden, a.eps, red);
-    const int nvec = a.hidden / WVec<WT>::kElems;
+    if (warp == kConsumerWarps) {
+        if (lane == 0)
+            ring_produce(ring, items, R, kRow<WT>, [&](int i) { return (const void *)(e + (size_t)(r0 + i) * kHidden); },
+                         &a.st->fault);
+        return;
+    }
+    stage_norm(nw_s, a.norm);
+    pdl_wait();
+    float xr[kLaneX];
+    load_lane_vec<WT>(xr, a.x, lane);
+    consumers_sync();
+    rms_lane<WT>(xr, nw_s, a.eps, lane);
     Top2 t = top2_empty();
     bool bad = false;
-    for (int row = gwarp; row < a.vocab; row += nwarps) {
-        const WT *rows[1] = {e + (size_t)row * a.hidden};
-        float acc[1];
-        warp_rows_dot<WT, 1, UNROLL>(rows, xs, nvec, lane, acc);
-        if (lane == 0) a.logits[row] = acc[0];
-        bad |= !isfinite(acc[0]);
-        top2_insert(t, acc[0], row);
+    const int groups = (items + R - 1) / R;
+    for (int g = 0; g < groups; g++) {
+        if (!ring_acquire(ring, g, &a.st->fault)) break;
+        const int n = min(R, items - g * R);
+        const unsigned char *stage = ring.stage(g % kStages);
+#pragma unroll
+        for (int m = 0; m < R / kConsumerWarps; m++) {
+            const int j = warp + kConsumerWarps * m;
+            if (j < n) {
+                const int row = r0 + g * R + j;
+                const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
+                if (lane == 0) a.logits[row] = y;
+                bad |= !isfinite(y);
+                top2_insert(t, y, row);
+            }
+        }
+        ring_release(ring, g);
     }
-    // Warp results (identical in every lane) -> block result.
+    // Warp results (identical in every lane) -> CTA result -> last CTA merges.
     if (lane == 0) {
         sv[2 * warp] = t.a; sv[2 * warp + 1] = t.b;
         si[2 * warp] = t.ai; si[2 * warp + 1] = t.bi;
+        if (bad) atomicOr(&a.sync[1], 1u);
     }
-    const int any_bad = __syncthreads_or(bad);
+    consumers_sync();
     if (warp == 0) {
         Top2 u = top2_empty();
-        if (lane < (int)(blockDim.x >> 5)) {
+        if (lane < kConsumerWarps) {
             top2_insert(u, sv[2 * lane], si[2 * lane]);
             top2_insert(u, sv[2 * lane + 1], si[2 * lane + 1]);
         }
@@ -264,25 +508,24 @@ __global__ void __launch_bounds__(kBlock) readout_kernel(ReadoutArgs a) {
         if (lane == 0) {
             a.pv[2 * blockIdx.x] = u.a; a.pv[2 * blockIdx.x + 1] = u.b;
             a.pi[2 * blockIdx.x] = u.ai; a.pi[2 * blockIdx.x + 1] = u.bi;
-            if (any_bad) atomicOr(&a.sync[1], 1u);
             __threadfence();
             last = atomicAdd(&a.sync[0], 1u) == gridDim.x - 1;
         }
     }
-    __syncthreads();
+    consumers_sync();
     if (!last) return;
     __threadfence();
     Top2 u = top2_empty();
-    for (int i = threadIdx.x; i < 2 * (int)gridDim.x; i += blockDim.x) top2_insert(u, __ldcg(a.pv + i), __ldcg(a.pi + i));
+    for (int i = threadIdx.x; i < 2 * (int)gridDim.x; i += kConsumerWarps * 32) top2_insert(u, __ldcg(a.pv + i), __ldcg(a.pi + i));
     top2_merge_warp(u);
     if (lane == 0) {
         sv[2 * warp] = u.a; sv[2 * warp + 1] = u.b;
         si[2 * warp] = u.ai; si[2 * warp + 1] = u.bi;
     }
-    __syncthreads();
+    consumers_sync();
     if (warp == 0) {
         Top2 z = top2_empty();
-        if (lane < (int)(blockDim.x >> 5)) {
+        if (lane < kConsumerWarps) {
             top2_insert(z, sv[2 * lane], si[2 * lane]);
             top2_insert(z, sv[2 * lane + 1], si[2 * lane + 1]);
         }
@@ -310,22 +553,12 @@ __global__ void set_state_kernel(DecodeState *st, int token, int position) {
     st->position = position;
     st->step = 0;
     st->invalid = 0;
+    st->fault = 0u;
 }
 
-template <typename T> inline void set_smem(T *kernel, int bytes) {
-    TCM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+template <typename T> inline void set_smem(T *kernel, size_t bytes) {
+    TCM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
 }
-
-// GEMV shapes: 16-byte vectors in flight per row per lane (UNROLL) and warps
-// per row (KSPLIT). A 1536-wide FP32 row is 12 vectors per lane (one round of
-// loads); BF16 is 6. The 8960-wide down rows are split over 4 warps.
-template <typename WT> struct Tune;
-template <> struct Tune<float> {
-    static constexpr int kQkv = 12, kO = 12, kGateUp = 6, kRead = 12, kDownSplit = 4, kDown = 18;
-};
-template <> struct Tune<uint16_t> {
-    static constexpr int kQkv = 6, kO = 6, kGateUp = 6, kRead = 6, kDownSplit = 4, kDown = 9;
-};
 
 }  // namespace
 
@@ -367,17 +600,17 @@ struct QwenB200Runner {
     cudaGraphExec_t graph;
     bool graph_ready;
     bool after_host;  // the last stream operation was a host copy: next launch is not programmatic
-    int grid_gemv, launches;
+    int grid, launches;
 };
 
 namespace {
 
 template <typename WT> void setup_kernels_typed() {
-    set_smem(qkv_kernel<WT, Tune<WT>::kQkv>, 64 * 1024);
-    set_smem(residual_gemv_kernel<WT, 1, Tune<WT>::kO>, 96 * 1024);
-    set_smem(residual_gemv_kernel<WT, Tune<WT>::kDownSplit, Tune<WT>::kDown>, 96 * 1024);
-    set_smem(gateup_kernel<WT, Tune<WT>::kGateUp>, 64 * 1024);
-    set_smem(readout_kernel<WT, Tune<WT>::kRead>, 64 * 1024);
+    set_smem(qkv_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
+    set_smem(oproj_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
+    set_smem(gateup_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
+    set_smem(down_kernel<WT>, ring_smem_bytes(kDownStages, kDownStage<WT>));
+    set_smem(readout_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
 }
 void setup_kernels() {
     static std::once_flag once;
@@ -405,41 +638,28 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.kcache = has_dense(r, layer) ? r->b.keys + slot_offset(r, layer) : nullptr;
     a.vcache = has_dense(r, layer) ? r->b.values + slot_offset(r, layer) : nullptr;
     a.st = r->st;
-    a.hidden = s.hidden; a.qheads = s.qheads; a.kvheads = s.kvheads; a.capacity = r->b.capacity; a.eps = s.epsilon;
-    const int tasks = (s.qheads + 2 * s.kvheads) * 64;
-    int grid = (tasks + kBlock / 32 - 1) / (kBlock / 32);
-    launch(qkv_kernel<WT, Tune<WT>::kQkv>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, a);
+    a.qheads = s.qheads; a.kvheads = s.kvheads; a.capacity = r->b.capacity; a.eps = s.epsilon;
+    launch(qkv_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
 }
 void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
-    AttnSource src = {};
-    src.keys = r->b.keys + slot_offset(r, layer);
-    src.values = r->b.values + slot_offset(r, layer);
-    attention_split(r->b.q, src, false, r->b.capacity, -1, &r->st->position, s.qheads, s.kvheads, kAttnSplits,
-                    r->attn_part, r->attn_counters, r->b.attention, stream(), pdl);
+    const float *keys = r->b.keys + slot_offset(r, layer), *values = r->b.values + slot_offset(r, layer);
+    launch(attn_decode_kernel<6>, dim3(kAttnSplits, s.kvheads), dim3(kDecodeAttnThreads), 0, stream(), pdl,
+           (const float *)r->b.q, keys, values, r->b.capacity, (const int *)&r->st->position, sqrtf((float)kHeadDim),
+           r->attn_part, r->attn_counters, r->b.attention);
 }
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
-    const QwenB200Shape &s = r->d->s;
-    const QwenB200Layer &L = r->d->layers[layer];
-    ResidualArgs o = {L.o, r->b.attention, r->b.x, s.qheads * s.head, s.hidden};
-    const int grid = (s.hidden + kBlock / 32 - 1) / (kBlock / 32);
-    launch(residual_gemv_kernel<WT, 1, Tune<WT>::kO>, dim3(grid), dim3(kBlock), (size_t)o.in_dim * 4, stream(), pdl, o);
+    ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st};
+    launch(oproj_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
 }
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
-    const QwenB200Shape &s = r->d->s;
     const QwenB200Layer &L = r->d->layers[layer];
-    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, s.hidden, s.intermediate, s.epsilon};
-    int grid = (s.intermediate + kBlock / 32 - 1) / (kBlock / 32);
-    if (grid > r->grid_gemv) grid = r->grid_gemv;
-    launch(gateup_kernel<WT, Tune<WT>::kGateUp>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, g);
+    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, r->st, r->d->s.epsilon};
+    launch(gateup_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
 }
 template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) {
-    const QwenB200Shape &s = r->d->s;
-    const QwenB200Layer &L = r->d->layers[layer];
-    ResidualArgs dn = {L.down, r->b.gate, r->b.x, s.intermediate, s.hidden};
-    constexpr int split = Tune<WT>::kDownSplit, rows_per_cta = (kBlock / 32) / split;
-    const int grid = (s.hidden + rows_per_cta - 1) / rows_per_cta;
-    launch(residual_gemv_kernel<WT, split, Tune<WT>::kDown>, dim3(grid), dim3(kBlock), (size_t)dn.in_dim * 4, stream(),
+    DownArgs dn = {r->d->layers[layer].down, r->b.gate, r->b.x, r->st};
+    launch(down_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kDownStages, kDownStage<WT>), stream(),
            pdl, dn);
 }
 template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl) {
@@ -449,12 +669,10 @@ template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl) {
 }
 template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
     const QwenB200Decoder *d = r->d;
-    const QwenB200Shape &s = d->s;
     ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, r->log,
-                     s.hidden, s.vocab, s.epsilon};
-    int grid = (s.vocab + kBlock / 32 - 1) / (kBlock / 32);
-    if (grid > r->grid_gemv) grid = r->grid_gemv;
-    launch(readout_kernel<WT, Tune<WT>::kRead>, dim3(grid), dim3(kBlock), (size_t)s.hidden * 4, stream(), pdl, a);
+                     d->s.vocab, d->s.epsilon};
+    launch(readout_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
+           a);
 }
 
 void launch_layer(QwenB200Runner *r, int layer, bool pdl_first) {
@@ -498,13 +716,18 @@ void write_state(QwenB200Runner *r, int token, int position) {
     r->host->position = position;
     r->host->step = 0;
     r->host->invalid = 0;
-    TCM_CUDA(cudaMemcpyAsync(r->st, r->host, 4 * sizeof(int), cudaMemcpyHostToDevice, stream()));
+    r->host->fault = 0u;
+    TCM_CUDA(cudaMemcpyAsync(r->st, r->host, 8 * sizeof(int), cudaMemcpyHostToDevice, stream()));
     r->after_host = true;
 }
 int read_top(QwenB200Runner *r, TcmTop2 *top) {
     TCM_CUDA(cudaMemcpyAsync(r->host, r->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream()));
     TCM_CUDA(cudaStreamSynchronize(stream()));
     if (top) *top = r->host->top;
+    if (r->host->fault) {
+        fprintf(stderr, "B200 decode: a pipeline wait ran out (fault bits 0x%x)\n", r->host->fault);
+        return -4;
+    }
     return r->host->invalid ? -3 : 0;
 }
 bool valid_token(const QwenB200Runner *r, int token, int position) {
@@ -520,9 +743,11 @@ extern "C" {
 QwenB200Decoder *qwen_b200_decoder_create(const QwenB200Shape *shape, const float *embedding,
                                           const float *final_norm, const QwenB200Layer *layers, int matrix_dtype) {
     const QwenB200Shape &s = *shape;
-    if (s.head != kHeadDim || s.kvheads < 1 || s.qheads % s.kvheads || s.qheads / s.kvheads > kAttnMaxGroup ||
-        s.hidden % 8 || s.intermediate % 8 || s.layers < 1 || s.vocab < 1 || s.qheads * s.head != s.hidden ||
-        s.hidden * 4 > 64 * 1024 || s.intermediate * 4 > 96 * 1024)
+    // The fused kernels are built for the Qwen2.5-1.5B geometry: hidden 1536, MLP
+    // 8960, head 128, six query heads per KV head. Other shapes use the primitives.
+    if (s.head != kHeadDim || s.hidden != kHidden || s.intermediate != kInter || s.kvheads < 1 ||
+        s.qheads * s.head != s.hidden || s.qheads != 6 * s.kvheads || s.layers < 1 || s.vocab < 1 ||
+        (s.qheads + 2 * s.kvheads) * 64 > kMaxPairsPerCta * 16)
         return nullptr;
     int dtype = matrix_dtype ? matrix_dtype : weight_dtype(embedding);
     if (dtype == 0) dtype = 1;
@@ -567,9 +792,9 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->attn_part = (float *)gpu_alloc(part * sizeof(float));
     r->attn_counters = (unsigned *)gpu_alloc((size_t)d->s.kvheads * sizeof(unsigned));
     gpu_zero(r->attn_counters, (size_t)d->s.kvheads * sizeof(unsigned));
-    r->grid_gemv = sm_count() * 2;
-    r->top_pv = (float *)gpu_alloc((size_t)2 * r->grid_gemv * sizeof(float));
-    r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid_gemv * sizeof(int));
+    r->grid = sm_count();
+    r->top_pv = (float *)gpu_alloc((size_t)2 * r->grid * sizeof(float));
+    r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid * sizeof(int));
     r->sync = (unsigned *)gpu_alloc(2 * sizeof(unsigned));
     gpu_zero(r->sync, 2 * sizeof(unsigned));
     TCM_CUDA(cudaMallocHost((void **)&r->host, sizeof(DecodeState)));
