@@ -1,35 +1,38 @@
 // Decode attention for the fused path: split-K over the FP32 K/V cache with
 // every warp doing flash-decoding in registers.
 //
-// CTA (split, kv head) owns rows [t0, t1) (at least kAttnMinRows of them);
-// its four warps split those rows again. A lane holds 4 of the 128 head
+// CTA (split, kv head) owns rows [t0, t1) (at least kAttnMinRows of them); its
+// eight warps split those rows again. A lane holds 4 of the 128 head
 // dimensions: per step of four rows it loads the K and V rows (512-byte
-// coalesced reads, nothing staged in shared memory), forms the six query
-// heads' partial dots, reduces them across the warp, and updates each head's
-// running max, rescaled sum and accumulator. Warps then merge in a fixed order,
-// each CTA publishes (m, l, acc) per head, and the last CTA of the KV head
-// combines the slices in split order (deterministic). Scores are dot / sqrt(128)
-// as in the reference's CPU path (tests/gpu_stub.c:166).
+// coalesced reads, nothing staged in shared memory), forms the query heads'
+// partial dots, reduces them across the warp, and updates each head's running
+// max, rescaled sum and accumulator. The warps merge in a fixed order, each CTA
+// publishes (m, l, acc) per head, and the last CTA of the KV head combines the
+// slices: every warp sums a fixed subset of slices with independent vector
+// loads, then the warp sums meet in shared memory in warp order (deterministic).
+// Scores are dot * (1 / sqrt(128)), the reference's GPU scaling
+// (src/qwen_cuda.cu:70).
 #pragma once
 #include "common.cuh"
 #include "attention.cuh"
 
 namespace tcm {
 
-constexpr int kDecodeAttnWarps = 4;
+constexpr int kDecodeAttnWarps = 8;
 constexpr int kDecodeAttnThreads = kDecodeAttnWarps * 32;
 
 template <int G>
-__global__ void __launch_bounds__(kDecodeAttnThreads) attn_decode_kernel(
+__global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
-    const int *__restrict__ position, float sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
+    const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
     float *__restrict__ out) {
+    static_assert(G <= kDecodeAttnWarps, "one warp per query head in the combine");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
     __shared__ float slice_w[kAttnSplits][G];
     __shared__ float den_s[G];
     __shared__ int last_s;
-    const int kvh = blockIdx.y, split = blockIdx.x, kvheads = gridDim.y;
+    const int kvh = blockIdx.y, split = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait();
     pdl_trigger();
@@ -82,7 +85,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads) attn_decode_kernel(
             float mx = m[g];
 #pragma unroll
             for (int i = 0; i < kStep; i++) {
-                s[i][g] = t + i < r1 ? __fdiv_rn(s[i][g], sqrt_dim) : -INFINITY;
+                s[i][g] = t + i < r1 ? s[i][g] * inv_sqrt_dim : -INFINITY;
                 mx = fmaxf(mx, s[i][g]);
             }
             const float c = m[g] == -INFINITY ? 0.f : expf(m[g] - mx);
@@ -102,7 +105,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads) attn_decode_kernel(
             m[g] = mx;
         }
     }
-    // Merge the four warps (fixed order) into this CTA's slice result.
+    // Merge the warps (fixed order) into this CTA's slice result.
 #pragma unroll
     for (int g = 0; g < G; g++) {
         reinterpret_cast<float4 *>(wacc[warp][g])[lane] = acc[g];
@@ -113,26 +116,23 @@ __global__ void __launch_bounds__(kDecodeAttnThreads) attn_decode_kernel(
     }
     __syncthreads();
     float *mine = part + ((size_t)kvh * nsplit + split) * kAttnPartialFloats;
-    {
-        const int d = tid;  // 128 threads, one head dimension each
+    for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
+        const int g = o / kHeadDim, d = o % kHeadDim;
+        float M = -INFINITY;
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            float M = -INFINITY;
+        for (int w = 0; w < kDecodeAttnWarps; w++) M = fmaxf(M, wm[w][g]);
+        float num = 0.f, den = 0.f;
 #pragma unroll
-            for (int w = 0; w < kDecodeAttnWarps; w++) M = fmaxf(M, wm[w][g]);
-            float num = 0.f, den = 0.f;
-#pragma unroll
-            for (int w = 0; w < kDecodeAttnWarps; w++) {
-                if (wm[w][g] == -INFINITY) continue;
-                const float e = expf(wm[w][g] - M);
-                den = fmaf(e, wl[w][g], den);
-                num = fmaf(e, wacc[w][g][d], num);
-            }
-            mine[2 * kAttnMaxGroup + g * kHeadDim + d] = num;
-            if (d == 0) {
-                mine[g] = M;
-                mine[kAttnMaxGroup + g] = den;
-            }
+        for (int w = 0; w < kDecodeAttnWarps; w++) {
+            if (wm[w][g] == -INFINITY) continue;
+            const float e = expf(wm[w][g] - M);
+            den = fmaf(e, wl[w][g], den);
+            num = fmaf(e, wacc[w][g][d], num);
+        }
+        mine[2 * kAttnMaxGroup + g * kHeadDim + d] = num;
+        if (d == 0) {
+            mine[g] = M;
+            mine[kAttnMaxGroup + g] = den;
         }
     }
     __threadfence();
@@ -141,39 +141,54 @@ __global__ void __launch_bounds__(kDecodeAttnThreads) attn_decode_kernel(
     __syncthreads();
     if (!last_s) return;
     __threadfence();
-    // Last CTA of this KV head: weights exp(m_s - M) per slice, then every
-    // (head, dimension) sums its slices in split order.
     const float *all = part + (size_t)kvh * nsplit * kAttnPartialFloats;
-    if (warp == 0) {
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float M = -INFINITY;
-            for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(all + (size_t)s * kAttnPartialFloats + g));
-            M = warp_max(M);
-            float den = 0.f;
-            for (int s = lane; s < nsplit; s += 32) {
-                const float *p = all + (size_t)s * kAttnPartialFloats;
-                const float ms = __ldcg(p + g);
-                const float w = ms == -INFINITY ? 0.f : expf(ms - M);
-                slice_w[s][g] = w;
-                den = fmaf(w, __ldcg(p + kAttnMaxGroup + g), den);
-            }
-            den = warp_sum(den);
-            if (lane == 0) den_s[g] = den;
+    // Slice weights: warp g owns query head g.
+    if (warp < G) {
+        const int g = warp;
+        float M = -INFINITY;
+        for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(all + (size_t)s * kAttnPartialFloats + g));
+        M = warp_max(M);
+        float den = 0.f;
+        for (int s = lane; s < nsplit; s += 32) {
+            const float *p = all + (size_t)s * kAttnPartialFloats;
+            const float ms = __ldcg(p + g);
+            const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+            slice_w[s][g] = w;
+            den = fmaf(w, __ldcg(p + kAttnMaxGroup + g), den);
         }
+        den = warp_sum(den);
+        if (lane == 0) den_s[g] = den;
     }
     __syncthreads();
-    const int d = tid;
+    // Warp w sums slices w, w + 8, ... for all heads; lane owns dims 4*lane..+3.
+    float4 sum[G];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        const float *p = all + 2 * kAttnMaxGroup + g * kHeadDim + d;
+    for (int g = 0; g < G; g++) sum[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = warp; s < nsplit; s += kDecodeAttnWarps) {
+        const float4 *p = reinterpret_cast<const float4 *>(all + (size_t)s * kAttnPartialFloats + 2 * kAttnMaxGroup);
+        float4 v[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) v[g] = __ldcg(p + g * (kHeadDim / 4) + lane);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float w = slice_w[s][g];
+            sum[g].x = fmaf(w, v[g].x, sum[g].x);
+            sum[g].y = fmaf(w, v[g].y, sum[g].y);
+            sum[g].z = fmaf(w, v[g].z, sum[g].z);
+            sum[g].w = fmaf(w, v[g].w, sum[g].w);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) reinterpret_cast<float4 *>(wacc[warp][g])[lane] = sum[g];
+    __syncthreads();
+    for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
+        const int g = o / kHeadDim, d = o % kHeadDim;
         float num = 0.f;
-#pragma unroll 8
-        for (int s = 0; s < nsplit; s++) num = fmaf(slice_w[s][g], __ldcg(p + (size_t)s * kAttnPartialFloats), num);
+#pragma unroll
+        for (int w = 0; w < kDecodeAttnWarps; w++) num += wacc[w][g][d];
         out[((size_t)kvh * G + g) * kHeadDim + d] = __fdiv_rn(num, den_s[g]);
     }
     if (tid == 0) counters[kvh] = 0u;
-    (void)kvheads;
 }
 
 }  // namespace tcm

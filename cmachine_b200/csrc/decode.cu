@@ -645,7 +645,7 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
     const float *keys = r->b.keys + slot_offset(r, layer), *values = r->b.values + slot_offset(r, layer);
     launch(attn_decode_kernel<6>, dim3(kAttnSplits, s.kvheads), dim3(kDecodeAttnThreads), 0, stream(), pdl,
-           (const float *)r->b.q, keys, values, r->b.capacity, (const int *)&r->st->position, sqrtf((float)kHeadDim),
+           (const float *)r->b.q, keys, values, r->b.capacity, (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim),
            r->attn_part, r->attn_counters, r->b.attention);
 }
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
