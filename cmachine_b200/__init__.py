@@ -117,6 +117,8 @@ def _declare(L, strict: bool = True):
         "qwen_b200_decoder_weight_bytes": (c_size_t, [P]),
         "qwen_b200_launches_per_token": (c_int, [P]),
         "qwen_b200_time_stage": (c_float, [P, c_int, c_int, c_int, c_int]),
+        "qwen_b200_trace": (c_int, [P, c_int]),
+        "qwen_b200_trace_read": (c_int, [P, P, c_size_t]),
         "qwen_b200_enqueue": (c_int, [P, c_int, c_int, c_int]),
         "qwen_b200_last": (c_int, [P, POINTER(Top2)]),
         "qwen_b200_generate": (c_int, [P, c_int, c_int, c_int, POINTER(c_int), POINTER(Top2)]),

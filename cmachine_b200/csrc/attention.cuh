@@ -21,6 +21,7 @@ constexpr int kAttnMaxGroup = 8;   // query heads per KV head
 constexpr int kAttnSplits = 74;    // slices per KV head: 2 KV heads x 74 = 148 CTAs, one per SM
 constexpr int kAttnMinRows = 64;   // fewest cache rows per slice
 static_assert(kAttnSplits * kAttnMaxGroup <= 2 * kAttnTile * kHeadDim, "slice weights must fit a tile buffer");
+static_assert(kAttnSplits <= 96, "the decode combine holds at most three slices per lane");
 constexpr int kAttnPerThread = kAttnMaxGroup * kHeadDim / kAttnThreads;
 
 // Floats of one slice's partial result: m[8], l[8], acc[8][128].

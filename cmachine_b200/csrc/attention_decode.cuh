@@ -18,6 +18,12 @@
 
 namespace tcm {
 
+__device__ __forceinline__ unsigned long long attn_clock() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 constexpr int kDecodeAttnWarps = 8;
 constexpr int kDecodeAttnThreads = kDecodeAttnWarps * 32;
 
@@ -25,7 +31,7 @@ template <int G>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
     const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
-    float *__restrict__ out) {
+    float *__restrict__ out, unsigned long long *__restrict__ trace) {
     static_assert(G <= kDecodeAttnWarps, "one warp per query head in the combine");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
@@ -34,7 +40,11 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     __shared__ int last_s;
     const int kvh = blockIdx.y, split = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // Timeline trace (optional): entry, wait released, slice done, CTA done.
+    unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
+    if (mark && tid == 0) mark[0] = attn_clock();
     pdl_wait();
+    if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
     const int L = min(*position + 1, capacity);
     const int chunk = max((L + (int)gridDim.x - 1) / (int)gridDim.x, kAttnMinRows);
@@ -105,6 +115,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
             m[g] = mx;
         }
     }
+    if (mark && tid == 0) mark[2] = attn_clock();
     // Merge the warps (fixed order) into this CTA's slice result.
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -139,22 +150,33 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     __syncthreads();
     if (tid == 0) last_s = atomicAdd(&counters[kvh], 1u) == (unsigned)(nsplit - 1);
     __syncthreads();
-    if (!last_s) return;
+    if (!last_s) {
+        if (mark && tid == 0) mark[3] = attn_clock();
+        return;
+    }
     __threadfence();
     const float *all = part + (size_t)kvh * nsplit * kAttnPartialFloats;
-    // Slice weights: warp g owns query head g.
+    // Slice weights: warp g owns query head g; one pass of independent loads
+    // (a lane holds at most three slices: nsplit <= kAttnSplits <= 96).
     if (warp < G) {
         const int g = warp;
+        float ms[3], ls[3];
         float M = -INFINITY;
-        for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(all + (size_t)s * kAttnPartialFloats + g));
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int s = lane + 32 * k;
+            ms[k] = s < nsplit ? __ldcg(all + (size_t)s * kAttnPartialFloats + g) : -INFINITY;
+            ls[k] = s < nsplit ? __ldcg(all + (size_t)s * kAttnPartialFloats + kAttnMaxGroup + g) : 0.f;
+            M = fmaxf(M, ms[k]);
+        }
         M = warp_max(M);
         float den = 0.f;
-        for (int s = lane; s < nsplit; s += 32) {
-            const float *p = all + (size_t)s * kAttnPartialFloats;
-            const float ms = __ldcg(p + g);
-            const float w = ms == -INFINITY ? 0.f : expf(ms - M);
-            slice_w[s][g] = w;
-            den = fmaf(w, __ldcg(p + kAttnMaxGroup + g), den);
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int s = lane + 32 * k;
+            const float w = ms[k] == -INFINITY ? 0.f : expf(ms[k] - M);
+            if (s < nsplit) slice_w[s][g] = w;
+            den = fmaf(w, ls[k], den);
         }
         den = warp_sum(den);
         if (lane == 0) den_s[g] = den;
@@ -164,6 +186,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     float4 sum[G];
 #pragma unroll
     for (int g = 0; g < G; g++) sum[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
     for (int s = warp; s < nsplit; s += kDecodeAttnWarps) {
         const float4 *p = reinterpret_cast<const float4 *>(all + (size_t)s * kAttnPartialFloats + 2 * kAttnMaxGroup);
         float4 v[G];
@@ -189,6 +212,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
         out[((size_t)kvh * G + g) * kHeadDim + d] = __fdiv_rn(num, den_s[g]);
     }
     if (tid == 0) counters[kvh] = 0u;
+    if (mark && tid == 0) mark[3] = attn_clock();
 }
 
 }  // namespace tcm

@@ -141,12 +141,20 @@ template <typename WT> __device__ __forceinline__ float row_dot(const unsigned c
 }
 __device__ __forceinline__ int share_begin(int total, int part, int parts) { return (int)((long long)part * total / parts); }
 
+// Optional timeline trace: thread 0 of each CTA stamps the global timer at
+// entry (0), when griddepcontrol.wait returned (1), when the input vector is
+// ready (2) and when its last group is done (3).
+__device__ __forceinline__ void trace_mark(unsigned long long *trace, int event) {
+    if (trace && threadIdx.x == 0) trace[(size_t)blockIdx.x * 4 + event] = global_ns();
+}
+
 // ---------------------------------------------------------------- stage 1: q/k/v
 struct QkvArgs {
     const void *wq, *wk, *wv, *embed;
     const float *bq, *bk, *bv, *norm, *rope_den;
     float *x, *q, *k, *v, *kcache, *vcache;
     DecodeState *st;
+    unsigned long long *trace;  // per-CTA timestamps of this launch, or null
     int qheads, kvheads, capacity;
     float eps;
 };
@@ -177,6 +185,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
     };
     if (threadIdx.x == 0) fail_s = 0;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
+    trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
@@ -194,6 +203,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
     }
     if (threadIdx.x < kHeadDim / 2) den_s[threadIdx.x] = a.rope_den[threadIdx.x];
     pdl_wait();
+    trace_mark(a.trace, 1);
     const int pos = a.st->position;
     float xr[kLaneX];
     if (a.embed) {
@@ -204,6 +214,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
     }
     consumers_sync();
     rms_lane<WT>(xr, nw_s, a.eps, lane);
+    trace_mark(a.trace, 2);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
         const int n = min(R, items - g * R);
@@ -248,6 +259,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
             }
         }
     }
+    trace_mark(a.trace, 3);
 }
 
 // ---------------------------------------------------------------- stage 3: O projection + residual
@@ -256,6 +268,7 @@ struct ORowsArgs {
     const float *in;
     float *x;
     DecodeState *st;
+    unsigned long long *trace;  // per-CTA timestamps of this launch, or null
 };
 template <typename WT>
 __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
@@ -266,6 +279,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
     const int items = r1 - r0;
     const WT *w = (const WT *)a.w;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
+    trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
@@ -274,8 +288,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
         return;
     }
     pdl_wait();
+    trace_mark(a.trace, 1);
     float xr[kLaneX];
     load_lane_vec<WT>(xr, a.in, lane);
+    trace_mark(a.trace, 2);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
         if (!ring_acquire(ring, g, &a.st->fault)) break;
@@ -291,6 +307,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
         }
         ring_release(ring, g);
     }
+    trace_mark(a.trace, 3);
 }
 
 // ---------------------------------------------------------------- stage 4: gate/up + SwiGLU
@@ -299,6 +316,7 @@ struct GateUpArgs {
     const float *norm, *x;
     float *h;
     DecodeState *st;
+    unsigned long long *trace;  // per-CTA timestamps of this launch, or null
     float eps;
 };
 // Items alternate gate row j, up row j; the epilogue forms h_j = silu(g) * u
@@ -316,6 +334,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     const WT *wg = (const WT *)a.wg, *wu = (const WT *)a.wu;
     if (threadIdx.x == 0) fail_s = 0;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
+    trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
@@ -326,10 +345,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     }
     stage_norm(nw_s, a.norm);
     pdl_wait();
+    trace_mark(a.trace, 1);
     float xr[kLaneX];
     load_lane_vec<WT>(xr, a.x, lane);
     consumers_sync();
     rms_lane<WT>(xr, nw_s, a.eps, lane);
+    trace_mark(a.trace, 2);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
         const int n = min(R, items - g * R);
@@ -355,6 +376,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
             a.h[j0 + (g * R) / 2 + t] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv);
         }
     }
+    trace_mark(a.trace, 3);
 }
 
 // ---------------------------------------------------------------- stage 5: down projection + residual
@@ -363,6 +385,7 @@ struct DownArgs {
     const float *h;
     float *x;
     DecodeState *st;
+    unsigned long long *trace;  // per-CTA timestamps of this launch, or null
 };
 // A stage holds RD rows of 8960; 8 / RD warps split each row into contiguous
 // pieces of 280 vectors; the pieces are summed in order into the residual.
@@ -381,6 +404,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
     const WT *w = (const WT *)a.w;
     if (threadIdx.x == 0) fail_s = 0;
     const Ring ring = ring_setup(smem, kDownStages, kDownStage<WT>);
+    trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
@@ -389,6 +413,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
         return;
     }
     pdl_wait();
+    trace_mark(a.trace, 1);
     float hr[KV * E];
 #pragma unroll
     for (int k = 0; k < KV; k++) {
@@ -403,6 +428,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
             hr[E * k + e + 3] = f.w;
         }
     }
+    trace_mark(a.trace, 2);
     const int groups = (items + RD - 1) / RD;
     for (int g = 0; g < groups; g++) {
         const int n = min(RD, items - g * RD);
@@ -430,6 +456,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
             a.x[row] = __fadd_rn(a.x[row], sum);
         }
     }
+    trace_mark(a.trace, 3);
 }
 
 // ---------------------------------------------------------------- readout + greedy top-2
@@ -441,6 +468,7 @@ struct ReadoutArgs {
     int *pi;
     unsigned *sync;  // [0] block counter, [1] non-finite flag
     DecodeState *st;
+    unsigned long long *trace;  // per-CTA timestamps of this launch, or null
     TcmTop2 *log;
     int vocab;
     float eps;
@@ -458,6 +486,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     const int items = r1 - r0;
     const WT *e = (const WT *)a.embed;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
+    trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
@@ -467,12 +496,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     }
     stage_norm(nw_s, a.norm);
     pdl_wait();
+    trace_mark(a.trace, 1);
     float xr[kLaneX];
     load_lane_vec<WT>(xr, a.x, lane);
     consumers_sync();
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     Top2 t = top2_empty();
     bool bad = false;
+    trace_mark(a.trace, 2);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
         if (!ring_acquire(ring, g, &a.st->fault)) break;
@@ -491,6 +522,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
         }
         ring_release(ring, g);
     }
+    trace_mark(a.trace, 3);
     // Warp results (identical in every lane) -> CTA result -> last CTA merges.
     if (lane == 0) {
         sv[2 * warp] = t.a; sv[2 * warp + 1] = t.b;
@@ -600,6 +632,8 @@ struct QwenB200Runner {
     cudaGraphExec_t graph;
     bool graph_ready;
     bool after_host;  // the last stream operation was a host copy: next launch is not programmatic
+    unsigned long long *trace;  // timeline buffer (kTraceLaunches x kTraceCtas x 4) or null
+    int trace_next;
     int grid, launches;
 };
 
@@ -618,6 +652,13 @@ void setup_kernels() {
         setup_kernels_typed<float>();
         setup_kernels_typed<uint16_t>();
     });
+}
+
+constexpr int kTraceLaunches = 160, kTraceCtas = 160;
+// The trace slot of the next launch (launch order within a token), or null.
+unsigned long long *trace_slot(QwenB200Runner *r) {
+    if (!r->trace) return nullptr;
+    return r->trace + (size_t)(r->trace_next++ % kTraceLaunches) * kTraceCtas * 4;
 }
 
 bool has_dense(const QwenB200Runner *r, int layer) { return r->slots[layer] >= 0; }
@@ -639,6 +680,7 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.vcache = has_dense(r, layer) ? r->b.values + slot_offset(r, layer) : nullptr;
     a.st = r->st;
     a.qheads = s.qheads; a.kvheads = s.kvheads; a.capacity = r->b.capacity; a.eps = s.epsilon;
+    a.trace = trace_slot(r);
     launch(qkv_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
 }
 void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
@@ -646,19 +688,19 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     const float *keys = r->b.keys + slot_offset(r, layer), *values = r->b.values + slot_offset(r, layer);
     launch(attn_decode_kernel<6>, dim3(kAttnSplits, s.kvheads), dim3(kDecodeAttnThreads), 0, stream(), pdl,
            (const float *)r->b.q, keys, values, r->b.capacity, (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim),
-           r->attn_part, r->attn_counters, r->b.attention);
+           r->attn_part, r->attn_counters, r->b.attention, trace_slot(r));
 }
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
-    ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st};
+    ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st, trace_slot(r)};
     launch(oproj_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
 }
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Layer &L = r->d->layers[layer];
-    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, r->st, r->d->s.epsilon};
+    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, r->st, trace_slot(r), r->d->s.epsilon};
     launch(gateup_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
 }
 template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) {
-    DownArgs dn = {r->d->layers[layer].down, r->b.gate, r->b.x, r->st};
+    DownArgs dn = {r->d->layers[layer].down, r->b.gate, r->b.x, r->st, trace_slot(r)};
     launch(down_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kDownStages, kDownStage<WT>), stream(),
            pdl, dn);
 }
@@ -669,8 +711,8 @@ template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl) {
 }
 template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
     const QwenB200Decoder *d = r->d;
-    ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, r->log,
-                     d->s.vocab, d->s.epsilon};
+    ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, trace_slot(r),
+                     r->log, d->s.vocab, d->s.epsilon};
     launch(readout_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
            a);
 }
@@ -807,6 +849,7 @@ void qwen_b200_runner_free(QwenB200Runner *r) {
     if (!r) return;
     TCM_CUDA(cudaStreamSynchronize(stream()));
     if (r->graph_ready) TCM_CUDA(cudaGraphExecDestroy(r->graph));
+    gpu_free(r->trace);
     gpu_free(r->st);
     gpu_free(r->log);
     gpu_free(r->attn_part);
@@ -890,6 +933,33 @@ int qwen_b200_generate(QwenB200Runner *r, int token, int position, int n, int *i
 }
 
 int qwen_b200_launches_per_token(const QwenB200Runner *r) { return r ? r->launches : 0; }
+
+int qwen_b200_trace(QwenB200Runner *r, int enable) {
+    if (!r) return -1;
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    if (r->graph_ready) {
+        TCM_CUDA(cudaGraphExecDestroy(r->graph));
+        r->graph_ready = false;
+    }
+    if (r->trace) {
+        gpu_free(r->trace);
+        r->trace = nullptr;
+    }
+    if (enable) {
+        const size_t bytes = (size_t)kTraceLaunches * kTraceCtas * 4 * sizeof(unsigned long long);
+        r->trace = (unsigned long long *)gpu_alloc(bytes);
+        gpu_zero(r->trace, bytes);
+    }
+    r->trace_next = 0;
+    return 0;
+}
+
+int qwen_b200_trace_read(QwenB200Runner *r, unsigned long long *host, size_t count) {
+    const size_t total = (size_t)kTraceLaunches * kTraceCtas * 4;
+    if (!r || !r->trace || count < total) return -1;
+    gpu_read(host, r->trace, total * sizeof(unsigned long long));
+    return r->trace_next;
+}
 
 float qwen_b200_time_stage(QwenB200Runner *r, int stage, int layer, int position, int reps) {
     if (!r || stage < 0 || stage > 5 || layer < 0 || layer >= r->d->s.layers || reps < 1 ||

@@ -1,0 +1,77 @@
+"""Timeline of one fused decode token (qwen_b200_trace): where the time goes
+between and inside the 141 launches of a token.
+
+    python -m cmachine_b200.trace_decode --profile 0 --prompt 512 --tokens 8
+
+Every CTA of every launch stamps the GPU global timer at entry, when its
+dependency on the previous launch was released (griddepcontrol.wait), when its
+input vector was ready and when it finished. Per stage kind the report gives the
+mean over layers of: the gap from the previous launch's last finish to this
+launch's first release (boundary), release to input ready, ready to last
+finish, and the whole span; then the token's total.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+
+import numpy as np
+
+import cmachine_b200 as cm
+
+LAUNCHES, CTAS = 160, 160
+STAGES = ["qkv", "attention", "oproj", "gateup", "down"]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--profile", type=int, choices=[0, 2], default=0)
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--tokens", type=int, default=8)
+    args = ap.parse_args()
+    L = cm.lib()
+    model = cm.Model(cm.qwen_shape(args.layers, 32768), 2026, cm.BENCH_LAW, args.profile)
+    s = cm.Session(model, args.prompt + args.tokens + 1)
+    for i in range(args.prompt):
+        assert s.push((i * 7919 + 11) % model.shape.vocab) == 0
+    runner = s.runner
+    assert L.qwen_b200_trace(runner, 1) == 0
+    status, _ = s.generate(args.tokens)
+    assert status == 0
+    buf = np.zeros(LAUNCHES * CTAS * 4, np.uint64)
+    n = L.qwen_b200_trace_read(runner, ctypes.c_void_p(buf.ctypes.data), buf.size)
+    L.qwen_b200_trace(runner, 0)
+    t = buf.reshape(LAUNCHES, CTAS, 4).astype(np.float64)
+    per_token = args.layers * 5 + 1
+    t0 = np.min(t[0, :, 0][t[0, :, 0] > 0])
+    rows = []
+    prev_done = None
+    for k in range(per_token):
+        m = t[k]
+        live = m[:, 0] > 0
+        entry = m[live, 0] - t0
+        rel = m[live, 1] - t0
+        ready = m[m[:, 2] > 0, 2] - t0
+        done = m[m[:, 3] > 0, 3] - t0
+        kind = "readout" if k == per_token - 1 else STAGES[k % 5]
+        rec = dict(kind=kind, entry0=entry.min(), release0=rel.min(), ready1=ready.max() if ready.size else np.nan,
+                   done1=done.max() if done.size else np.nan)
+        rec["boundary"] = rec["release0"] - prev_done if prev_done is not None else np.nan
+        prev_done = rec["done1"]
+        rows.append(rec)
+    print(f"launches recorded: {n}; token span {rows[-1]['done1'] / 1000:.1f} us")
+    print(f"{'stage':10s} {'boundary':>9s} {'rel->ready':>10s} {'ready->done':>11s} {'span':>8s}   (us, mean over layers)")
+    for kind in STAGES + ["readout"]:
+        sel = [r for r in rows if r["kind"] == kind]
+        b = np.nanmean([r["boundary"] for r in sel]) / 1000
+        rr = np.nanmean([r["ready1"] - r["release0"] for r in sel]) / 1000
+        rd = np.nanmean([r["done1"] - r["ready1"] for r in sel]) / 1000
+        sp = np.nanmean([r["done1"] - r["release0"] for r in sel]) / 1000
+        print(f"{kind:10s} {b:9.2f} {rr:10.2f} {rd:11.2f} {sp:8.2f}")
+    s.free()
+    model.free()
+
+
+if __name__ == "__main__":
+    main()

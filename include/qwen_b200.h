@@ -98,6 +98,14 @@ int qwen_b200_launches_per_token(const QwenB200Runner *);
  * 3 gate/up, 4 down, 5 readout) at `position`, over `reps` launches. */
 float qwen_b200_time_stage(QwenB200Runner *, int stage, int layer, int position, int reps);
 
+/* Timeline trace for performance work: with tracing on, every launch of a token
+ * stamps the GPU global timer per CTA at entry, dependency release, input ready
+ * and done (the whole-token graph is re-captured). trace_read copies the last
+ * token's stamps, 160 launches x 160 CTAs x 4 (zero where a CTA had no work),
+ * and returns the number of launches recorded. */
+int qwen_b200_trace(QwenB200Runner *, int enable);
+int qwen_b200_trace_read(QwenB200Runner *, unsigned long long *host, size_t count);
+
 /* CUDA-event timing on the library stream: record marks 0..15, elapsed ms. */
 void qwen_b200_mark(int index);
 float qwen_b200_elapsed_ms(int from, int to);
