@@ -26,9 +26,10 @@ __device__ __forceinline__ unsigned long long attn_clock() {
 
 constexpr int kDecodeAttnWarps = 8;
 constexpr int kDecodeAttnThreads = kDecodeAttnWarps * 32;
+constexpr int kDecodeMinRows = 32;  // fewest cache rows per CTA: one step of four rows per warp
 
 template <int G>
-__global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
+__global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
     const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
     float *__restrict__ out, unsigned long long *__restrict__ trace) {
@@ -47,7 +48,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
     const int L = min(*position + 1, capacity);
-    const int chunk = max((L + (int)gridDim.x - 1) / (int)gridDim.x, kAttnMinRows);
+    const int chunk = max((L + (int)gridDim.x - 1) / (int)gridDim.x, kDecodeMinRows);
     const int nsplit = (L + chunk - 1) / chunk;
     if (split >= nsplit) return;
     const int t0 = split * chunk, t1 = min(L, t0 + chunk);
@@ -65,15 +66,21 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
         m[g] = -INFINITY;
         l[g] = 0.f;
     }
+    // Rows in steps of four; the next step's K/V rows are loaded before this
+    // step's arithmetic so their latency overlaps it.
     constexpr int kStep = 4;
-    for (int t = r0; t < r1; t += kStep) {
-        float4 k4[kStep], v4[kStep];
+    float4 k4[kStep], v4[kStep], nk4[kStep], nv4[kStep];
+    auto load_rows = [&](int t, float4 (&kk)[kStep], float4 (&vv)[kStep]) {
 #pragma unroll
         for (int i = 0; i < kStep; i++) {
             const bool ok = t + i < r1;
-            k4[i] = ok ? __ldcg(kb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-            v4[i] = ok ? __ldcg(vb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+            kk[i] = ok ? __ldcg(kb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vv[i] = ok ? __ldcg(vb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+    };
+    if (r0 < r1) load_rows(r0, k4, v4);
+    for (int t = r0; t < r1; t += kStep) {
+        if (t + kStep < r1) load_rows(t + kStep, nk4, nv4);
         float s[kStep][G];
 #pragma unroll
         for (int i = 0; i < kStep; i++)
@@ -113,6 +120,11 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
             acc[g] = a;
             l[g] = fmaf(l[g], c, sum);
             m[g] = mx;
+        }
+#pragma unroll
+        for (int i = 0; i < kStep; i++) {
+            k4[i] = nk4[i];
+            v4[i] = nv4[i];
         }
     }
     if (mark && tid == 0) mark[2] = attn_clock();

@@ -55,20 +55,27 @@ def main():
         ready = m[m[:, 2] > 0, 2] - t0
         done = m[m[:, 3] > 0, 3] - t0
         kind = "readout" if k == per_token - 1 else STAGES[k % 5]
+        both = (m[:, 2] > 0) & (m[:, 1] > 0)
+        fin = (m[:, 3] > 0) & (m[:, 2] > 0)
         rec = dict(kind=kind, entry0=entry.min(), release0=rel.min(), ready1=ready.max() if ready.size else np.nan,
-                   done1=done.max() if done.size else np.nan)
+                   done1=done.max() if done.size else np.nan, release_spread=rel.max() - rel.min(),
+                   cta_ready=np.median(m[both, 2] - m[both, 1]) if both.any() else np.nan,
+                   cta_work=np.median(m[fin, 3] - m[fin, 2]) if fin.any() else np.nan,
+                   done_spread=(done.max() - done.min()) if done.size else np.nan)
         rec["boundary"] = rec["release0"] - prev_done if prev_done is not None else np.nan
         prev_done = rec["done1"]
         rows.append(rec)
     print(f"launches recorded: {n}; token span {rows[-1]['done1'] / 1000:.1f} us")
-    print(f"{'stage':10s} {'boundary':>9s} {'rel->ready':>10s} {'ready->done':>11s} {'span':>8s}   (us, mean over layers)")
+    print(f"{'stage':10s} {'boundary':>9s} {'rel->ready':>10s} {'ready->done':>11s} {'span':>8s} "
+          f"{'rel spread':>10s} {'cta ready':>9s} {'cta work':>9s} {'done spread':>11s}   (us, mean over layers)")
     for kind in STAGES + ["readout"]:
         sel = [r for r in rows if r["kind"] == kind]
         b = np.nanmean([r["boundary"] for r in sel]) / 1000
         rr = np.nanmean([r["ready1"] - r["release0"] for r in sel]) / 1000
         rd = np.nanmean([r["done1"] - r["ready1"] for r in sel]) / 1000
         sp = np.nanmean([r["done1"] - r["release0"] for r in sel]) / 1000
-        print(f"{kind:10s} {b:9.2f} {rr:10.2f} {rd:11.2f} {sp:8.2f}")
+        extra = [np.nanmean([r[k] for r in sel]) / 1000 for k in ("release_spread", "cta_ready", "cta_work", "done_spread")]
+        print(f"{kind:10s} {b:9.2f} {rr:10.2f} {rd:11.2f} {sp:8.2f} {extra[0]:10.2f} {extra[1]:9.2f} {extra[2]:9.2f} {extra[3]:11.2f}")
     s.free()
     model.free()
 
