@@ -6,10 +6,11 @@
 // dimensions: per step of four rows it loads the K and V rows (512-byte
 // coalesced reads, nothing staged in shared memory), forms the query heads'
 // partial dots, reduces them across the warp, and updates each head's running
-// max, rescaled sum and accumulator. The warps merge in a fixed order, each CTA
-// publishes (m, l, acc) per head, and the last CTA of the KV head combines the
-// slices: every warp sums a fixed subset of slices with independent vector
-// loads, then the warp sums meet in shared memory in warp order (deterministic).
+// max, rescaled sum and accumulator. The warps merge in a fixed order and each
+// CTA publishes (m, l, acc) per head. The slices then combine in two levels:
+// the last CTA to finish in each group of eight slices merges that group, and
+// the last group merges the groups, every merge loading one partial per warp
+// and folding the warps in order (deterministic).
 // Scores are dot * (1 / sqrt(128)), the reference's GPU scaling
 // (src/qwen_cuda.cu:70).
 #pragma once
@@ -28,6 +29,94 @@ constexpr int kDecodeAttnWarps = 8;
 constexpr int kDecodeAttnThreads = kDecodeAttnWarps * 32;
 constexpr int kDecodeMinRows = 32;  // fewest cache rows per CTA: one step of four rows per warp
 
+constexpr int kGroup = 8;       // slices merged by the first combine level
+constexpr int kMaxGroups = 16;  // >= ceil(kAttnSplits / kGroup)
+static_assert(kMaxGroups * kGroup >= kAttnSplits, "group table too small");
+
+// A warp's running softmax state per query head: max m, rescaled sum l, and
+// the lane's four accumulator dimensions.
+template <int G> __device__ __forceinline__ void state_reset(float (&m)[G], float (&l)[G], float4 (&acc)[G]) {
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+// Fold one published partial (m[8], l[8], acc[8][128]) into the warp state.
+template <int G>
+__device__ __forceinline__ void state_merge(float (&m)[G], float (&l)[G], float4 (&acc)[G], const float *p, int lane) {
+    float mp[G], lp[G];
+    float4 ap[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        mp[g] = __ldcg(p + g);
+        lp[g] = __ldcg(p + kAttnMaxGroup + g);
+        ap[g] = __ldcg(reinterpret_cast<const float4 *>(p + 2 * kAttnMaxGroup + g * kHeadDim) + lane);
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        if (mp[g] == -INFINITY) continue;
+        const float M = fmaxf(m[g], mp[g]);
+        const float cs = m[g] == -INFINITY ? 0.f : expf(m[g] - M), cp = expf(mp[g] - M);
+        l[g] = fmaf(l[g], cs, lp[g] * cp);
+        acc[g] = make_float4(fmaf(acc[g].x, cs, ap[g].x * cp), fmaf(acc[g].y, cs, ap[g].y * cp),
+                             fmaf(acc[g].z, cs, ap[g].z * cp), fmaf(acc[g].w, cs, ap[g].w * cp));
+        m[g] = M;
+    }
+}
+// Merge the eight warps' states in warp order; write a partial (m, l, acc) to
+// `partial`, or the normalised result acc / l to `out` ([G][128]).
+template <int G>
+__device__ __forceinline__ void cta_merge(const float (&m)[G], const float (&l)[G], const float4 (&acc)[G],
+                                          float (*wm)[G], float (*wl)[G], float (*wacc)[G][kHeadDim], float *partial,
+                                          float *out) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __syncthreads();  // the buffers may still be read by a previous merge
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        reinterpret_cast<float4 *>(wacc[warp][g])[lane] = acc[g];
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+    }
+    __syncthreads();
+    for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
+        const int g = o / kHeadDim, d = o % kHeadDim;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecodeAttnWarps; w++) M = fmaxf(M, wm[w][g]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecodeAttnWarps; w++) {
+            if (wm[w][g] == -INFINITY) continue;
+            const float e = expf(wm[w][g] - M);
+            den = fmaf(e, wl[w][g], den);
+            num = fmaf(e, wacc[w][g][d], num);
+        }
+        if (out) {
+            out[g * kHeadDim + d] = __fdiv_rn(num, den);
+        } else {
+            partial[2 * kAttnMaxGroup + g * kHeadDim + d] = num;
+            if (d == 0) {
+                partial[g] = M;
+                partial[kAttnMaxGroup + g] = den;
+            }
+        }
+    }
+}
+// Publish: fence, count this CTA in `counter`; true in the CTA that arrives last
+// of `expected` (all threads), which also sees every earlier CTA's writes.
+__device__ __forceinline__ bool last_arrival(unsigned *counter, int expected, int *flag) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *flag = atomicAdd(counter, 1u) == (unsigned)(expected - 1);
+    __syncthreads();
+    if (*flag) __threadfence();
+    return *flag != 0;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
@@ -36,8 +125,6 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
     static_assert(G <= kDecodeAttnWarps, "one warp per query head in the combine");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
-    __shared__ float slice_w[kAttnSplits][G];
-    __shared__ float den_s[G];
     __shared__ int last_s;
     const int kvh = blockIdx.y, split = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -128,102 +215,38 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
         }
     }
     if (mark && tid == 0) mark[2] = attn_clock();
-    // Merge the warps (fixed order) into this CTA's slice result.
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        reinterpret_cast<float4 *>(wacc[warp][g])[lane] = acc[g];
-        if (lane == 0) {
-            wm[warp][g] = m[g];
-            wl[warp][g] = l[g];
-        }
-    }
-    __syncthreads();
-    float *mine = part + ((size_t)kvh * nsplit + split) * kAttnPartialFloats;
-    for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
-        const int g = o / kHeadDim, d = o % kHeadDim;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kDecodeAttnWarps; w++) M = fmaxf(M, wm[w][g]);
-        float num = 0.f, den = 0.f;
-#pragma unroll
-        for (int w = 0; w < kDecodeAttnWarps; w++) {
-            if (wm[w][g] == -INFINITY) continue;
-            const float e = expf(wm[w][g] - M);
-            den = fmaf(e, wl[w][g], den);
-            num = fmaf(e, wacc[w][g][d], num);
-        }
-        mine[2 * kAttnMaxGroup + g * kHeadDim + d] = num;
-        if (d == 0) {
-            mine[g] = M;
-            mine[kAttnMaxGroup + g] = den;
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) last_s = atomicAdd(&counters[kvh], 1u) == (unsigned)(nsplit - 1);
-    __syncthreads();
-    if (!last_s) {
+    // This CTA's slice result, then a two-level combine: the last CTA of each
+    // group of kGroup slices merges the group, the last group merges the groups.
+    float *head_part = part + (size_t)kvh * (kAttnSplits + kMaxGroups) * kAttnPartialFloats;
+    cta_merge<G>(m, l, acc, wm, wl, wacc, head_part + (size_t)split * kAttnPartialFloats, nullptr);
+    const int ngroups = (nsplit + kGroup - 1) / kGroup, group = split / kGroup;
+    const int gsize = min(kGroup, nsplit - group * kGroup);
+    unsigned *head_counters = counters + (size_t)kvh * (kMaxGroups + 1);
+    if (!last_arrival(head_counters + 1 + group, gsize, &last_s)) {
         if (mark && tid == 0) mark[3] = attn_clock();
         return;
     }
-    __threadfence();
-    const float *all = part + (size_t)kvh * nsplit * kAttnPartialFloats;
-    // Slice weights: warp g owns query head g; one pass of independent loads
-    // (a lane holds at most three slices: nsplit <= kAttnSplits <= 96).
-    if (warp < G) {
-        const int g = warp;
-        float ms[3], ls[3];
-        float M = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 3; k++) {
-            const int s = lane + 32 * k;
-            ms[k] = s < nsplit ? __ldcg(all + (size_t)s * kAttnPartialFloats + g) : -INFINITY;
-            ls[k] = s < nsplit ? __ldcg(all + (size_t)s * kAttnPartialFloats + kAttnMaxGroup + g) : 0.f;
-            M = fmaxf(M, ms[k]);
-        }
-        M = warp_max(M);
-        float den = 0.f;
-#pragma unroll
-        for (int k = 0; k < 3; k++) {
-            const int s = lane + 32 * k;
-            const float w = ms[k] == -INFINITY ? 0.f : expf(ms[k] - M);
-            if (s < nsplit) slice_w[s][g] = w;
-            den = fmaf(w, ls[k], den);
-        }
-        den = warp_sum(den);
-        if (lane == 0) den_s[g] = den;
+    // Level 1: merge this group's slices (warp w takes slice w of the group).
+    state_reset<G>(m, l, acc);
+    if (warp < gsize) state_merge<G>(m, l, acc, head_part + (size_t)(group * kGroup + warp) * kAttnPartialFloats, lane);
+    if (ngroups == 1) {
+        cta_merge<G>(m, l, acc, wm, wl, wacc, nullptr, out + (size_t)kvh * G * kHeadDim);
+        if (tid == 0) head_counters[1 + group] = 0u;
+        if (mark && tid == 0) mark[3] = attn_clock();
+        return;
     }
-    __syncthreads();
-    // Warp w sums slices w, w + 8, ... for all heads; lane owns dims 4*lane..+3.
-    float4 sum[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) sum[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 2
-    for (int s = warp; s < nsplit; s += kDecodeAttnWarps) {
-        const float4 *p = reinterpret_cast<const float4 *>(all + (size_t)s * kAttnPartialFloats + 2 * kAttnMaxGroup);
-        float4 v[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) v[g] = __ldcg(p + g * (kHeadDim / 4) + lane);
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float w = slice_w[s][g];
-            sum[g].x = fmaf(w, v[g].x, sum[g].x);
-            sum[g].y = fmaf(w, v[g].y, sum[g].y);
-            sum[g].z = fmaf(w, v[g].z, sum[g].z);
-            sum[g].w = fmaf(w, v[g].w, sum[g].w);
-        }
+    cta_merge<G>(m, l, acc, wm, wl, wacc, head_part + (size_t)(kAttnSplits + group) * kAttnPartialFloats, nullptr);
+    if (tid == 0) head_counters[1 + group] = 0u;
+    if (!last_arrival(head_counters, ngroups, &last_s)) {
+        if (mark && tid == 0) mark[3] = attn_clock();
+        return;
     }
-#pragma unroll
-    for (int g = 0; g < G; g++) reinterpret_cast<float4 *>(wacc[warp][g])[lane] = sum[g];
-    __syncthreads();
-    for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
-        const int g = o / kHeadDim, d = o % kHeadDim;
-        float num = 0.f;
-#pragma unroll
-        for (int w = 0; w < kDecodeAttnWarps; w++) num += wacc[w][g][d];
-        out[((size_t)kvh * G + g) * kHeadDim + d] = __fdiv_rn(num, den_s[g]);
-    }
-    if (tid == 0) counters[kvh] = 0u;
+    // Level 2: merge the group results (warp w takes groups w and w + 8).
+    state_reset<G>(m, l, acc);
+    for (int gi = warp; gi < ngroups; gi += kDecodeAttnWarps)
+        state_merge<G>(m, l, acc, head_part + (size_t)(kAttnSplits + gi) * kAttnPartialFloats, lane);
+    cta_merge<G>(m, l, acc, wm, wl, wacc, nullptr, out + (size_t)kvh * G * kHeadDim);
+    if (tid == 0) head_counters[0] = 0u;
     if (mark && tid == 0) mark[3] = attn_clock();
 }
 

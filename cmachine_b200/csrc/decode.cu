@@ -830,10 +830,11 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->st = (DecodeState *)gpu_alloc(sizeof(DecodeState));
     gpu_zero(r->st, sizeof(DecodeState));
     r->log = (TcmTop2 *)gpu_alloc(kLogCap * sizeof(TcmTop2));
-    const size_t part = (size_t)d->s.kvheads * kAttnSplits * kAttnPartialFloats;
+    const size_t part = (size_t)d->s.kvheads * (kAttnSplits + kMaxGroups) * kAttnPartialFloats;
     r->attn_part = (float *)gpu_alloc(part * sizeof(float));
-    r->attn_counters = (unsigned *)gpu_alloc((size_t)d->s.kvheads * sizeof(unsigned));
-    gpu_zero(r->attn_counters, (size_t)d->s.kvheads * sizeof(unsigned));
+    const size_t counters = (size_t)d->s.kvheads * (kMaxGroups + 1) * sizeof(unsigned);
+    r->attn_counters = (unsigned *)gpu_alloc(counters);
+    gpu_zero(r->attn_counters, counters);
     r->grid = sm_count();
     r->top_pv = (float *)gpu_alloc((size_t)2 * r->grid * sizeof(float));
     r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid * sizeof(int));
