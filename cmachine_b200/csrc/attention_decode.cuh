@@ -1,21 +1,23 @@
-// Decode attention for the fused path: split-K over the FP32 K/V cache with
-// every warp doing flash-decoding in registers.
+// Decode attention for the fused path: one thread-block cluster per KV head,
+// flash-decoding in registers, the slices merged through distributed shared
+// memory.
 //
-// CTA (split, kv head) owns rows [t0, t1) (at least kAttnMinRows of them); its
-// eight warps split those rows again. A lane holds 4 of the 128 head
-// dimensions: per step of four rows it loads the K and V rows (512-byte
-// coalesced reads, nothing staged in shared memory), forms the query heads'
-// partial dots, reduces them across the warp, and updates each head's running
-// max, rescaled sum and accumulator. The warps merge in a fixed order and each
-// CTA publishes (m, l, acc) per head. The slices then combine in two levels:
-// the last CTA to finish in each group of eight slices merges that group, and
-// the last group merges the groups, every merge loading one partial per warp
-// and folding the warps in order (deterministic).
+// The kCluster CTAs of a KV head split its cache rows; each CTA's eight warps
+// split them again. A lane holds 4 of the 128 head dimensions: per step of
+// four rows it loads the K and V rows (512-byte coalesced reads; the next
+// step's rows are loaded before this step's arithmetic), forms the query
+// heads' partial dots, reduces them across the warp and updates each head's
+// running max, rescaled sum and accumulator. The warps merge in a fixed order
+// into the CTA's partial in shared memory; after a cluster barrier every CTA
+// reads all partials of the cluster (DSMEM) for its share of the outputs and
+// folds them in rank order (deterministic), and a second barrier keeps the
+// partials alive until all reads are done. No global atomics or fences.
 // Scores are dot * (1 / sqrt(128)), the reference's GPU scaling
 // (src/qwen_cuda.cu:70).
 #pragma once
 #include "common.cuh"
 #include "attention.cuh"
+#include <cooperative_groups.h>
 
 namespace tcm {
 
@@ -29,9 +31,7 @@ constexpr int kDecodeAttnWarps = 8;
 constexpr int kDecodeAttnThreads = kDecodeAttnWarps * 32;
 constexpr int kDecodeMinRows = 32;  // fewest cache rows per CTA: one step of four rows per warp
 
-constexpr int kGroup = 8;       // slices merged by the first combine level
-constexpr int kMaxGroups = 16;  // >= ceil(kAttnSplits / kGroup)
-static_assert(kMaxGroups * kGroup >= kAttnSplits, "group table too small");
+constexpr int kCluster = 16;  // CTAs per KV head (non-portable cluster size)
 
 // A warp's running softmax state per query head: max m, rescaled sum l, and
 // the lane's four accumulator dimensions.
@@ -106,27 +106,18 @@ __device__ __forceinline__ void cta_merge(const float (&m)[G], const float (&l)[
         }
     }
 }
-// Publish: fence, count this CTA in `counter`; true in the CTA that arrives last
-// of `expected` (all threads), which also sees every earlier CTA's writes.
-__device__ __forceinline__ bool last_arrival(unsigned *counter, int expected, int *flag) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) *flag = atomicAdd(counter, 1u) == (unsigned)(expected - 1);
-    __syncthreads();
-    if (*flag) __threadfence();
-    return *flag != 0;
-}
-
 template <int G>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
-    const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
-    float *__restrict__ out, unsigned long long *__restrict__ trace) {
+    const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ out,
+    unsigned long long *__restrict__ trace) {
     static_assert(G <= kDecodeAttnWarps, "one warp per query head in the combine");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
-    __shared__ int last_s;
-    const int kvh = blockIdx.y, split = blockIdx.x;
+    __shared__ __align__(16) float cta_part[kAttnPartialFloats];
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int kvh = blockIdx.y, split = (int)cluster.block_rank();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // Timeline trace (optional): entry, wait released, slice done, CTA done.
     unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
@@ -135,10 +126,8 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
     if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
     const int L = min(*position + 1, capacity);
-    const int chunk = max((L + (int)gridDim.x - 1) / (int)gridDim.x, kDecodeMinRows);
-    const int nsplit = (L + chunk - 1) / chunk;
-    if (split >= nsplit) return;
-    const int t0 = split * chunk, t1 = min(L, t0 + chunk);
+    const int chunk = (L + kCluster - 1) / kCluster;
+    const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
     const int per_warp = (t1 - t0 + kDecodeAttnWarps - 1) / kDecodeAttnWarps;
     const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
     const float4 *kb = reinterpret_cast<const float4 *>(keys + (size_t)kvh * capacity * kHeadDim);
@@ -215,38 +204,27 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
         }
     }
     if (mark && tid == 0) mark[2] = attn_clock();
-    // This CTA's slice result, then a two-level combine: the last CTA of each
-    // group of kGroup slices merges the group, the last group merges the groups.
-    float *head_part = part + (size_t)kvh * (kAttnSplits + kMaxGroups) * kAttnPartialFloats;
-    cta_merge<G>(m, l, acc, wm, wl, wacc, head_part + (size_t)split * kAttnPartialFloats, nullptr);
-    const int ngroups = (nsplit + kGroup - 1) / kGroup, group = split / kGroup;
-    const int gsize = min(kGroup, nsplit - group * kGroup);
-    unsigned *head_counters = counters + (size_t)kvh * (kMaxGroups + 1);
-    if (!last_arrival(head_counters + 1 + group, gsize, &last_s)) {
-        if (mark && tid == 0) mark[3] = attn_clock();
-        return;
+    // This CTA's slice result into shared memory, then the cluster combine.
+    cta_merge<G>(m, l, acc, wm, wl, wacc, cta_part, nullptr);
+    cluster.sync();
+    constexpr int kOutPer = G * kHeadDim / kCluster;
+    static_assert(G * kHeadDim % kCluster == 0 && kOutPer <= kDecodeAttnThreads, "cluster output split");
+    if (tid < kOutPer) {
+        const int o = split * kOutPer + tid, g = o / kHeadDim, d = o % kHeadDim;
+        float M = -INFINITY;
+        for (int r = 0; r < kCluster; r++) M = fmaxf(M, cluster.map_shared_rank(cta_part, r)[g]);
+        float num = 0.f, den = 0.f;
+        for (int r = 0; r < kCluster; r++) {
+            const float *p = cluster.map_shared_rank(cta_part, r);
+            const float mr = p[g];
+            if (mr == -INFINITY) continue;
+            const float e = expf(mr - M);
+            den = fmaf(e, p[kAttnMaxGroup + g], den);
+            num = fmaf(e, p[2 * kAttnMaxGroup + g * kHeadDim + d], num);
+        }
+        out[((size_t)kvh * G + g) * kHeadDim + d] = __fdiv_rn(num, den);
     }
-    // Level 1: merge this group's slices (warp w takes slice w of the group).
-    state_reset<G>(m, l, acc);
-    if (warp < gsize) state_merge<G>(m, l, acc, head_part + (size_t)(group * kGroup + warp) * kAttnPartialFloats, lane);
-    if (ngroups == 1) {
-        cta_merge<G>(m, l, acc, wm, wl, wacc, nullptr, out + (size_t)kvh * G * kHeadDim);
-        if (tid == 0) head_counters[1 + group] = 0u;
-        if (mark && tid == 0) mark[3] = attn_clock();
-        return;
-    }
-    cta_merge<G>(m, l, acc, wm, wl, wacc, head_part + (size_t)(kAttnSplits + group) * kAttnPartialFloats, nullptr);
-    if (tid == 0) head_counters[1 + group] = 0u;
-    if (!last_arrival(head_counters, ngroups, &last_s)) {
-        if (mark && tid == 0) mark[3] = attn_clock();
-        return;
-    }
-    // Level 2: merge the group results (warp w takes groups w and w + 8).
-    state_reset<G>(m, l, acc);
-    for (int gi = warp; gi < ngroups; gi += kDecodeAttnWarps)
-        state_merge<G>(m, l, acc, head_part + (size_t)(kAttnSplits + gi) * kAttnPartialFloats, lane);
-    cta_merge<G>(m, l, acc, wm, wl, wacc, nullptr, out + (size_t)kvh * G * kHeadDim);
-    if (tid == 0) head_counters[0] = 0u;
+    cluster.sync();
     if (mark && tid == 0) mark[3] = attn_clock();
 }
 

@@ -639,6 +639,9 @@ struct QwenB200Runner {
 
 namespace {
 
+void setup_attention() {
+    TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+}
 template <typename WT> void setup_kernels_typed() {
     set_smem(qkv_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
     set_smem(oproj_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
@@ -651,6 +654,7 @@ void setup_kernels() {
     std::call_once(once, [] {
         setup_kernels_typed<float>();
         setup_kernels_typed<uint16_t>();
+        setup_attention();
     });
 }
 
@@ -686,9 +690,23 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
 void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
     const float *keys = r->b.keys + slot_offset(r, layer), *values = r->b.values + slot_offset(r, layer);
-    launch(attn_decode_kernel<6>, dim3(kAttnSplits, s.kvheads), dim3(kDecodeAttnThreads), 0, stream(), pdl,
-           (const float *)r->b.q, keys, values, r->b.capacity, (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim),
-           r->attn_part, r->attn_counters, r->b.attention, trace_slot(r));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kCluster, s.kvheads);
+    cfg.blockDim = dim3(kDecodeAttnThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream();
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6>, (const float *)r->b.q, keys, values, r->b.capacity,
+                                (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim), r->b.attention,
+                                trace_slot(r)));
 }
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
     ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st, trace_slot(r)};
@@ -830,11 +848,8 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->st = (DecodeState *)gpu_alloc(sizeof(DecodeState));
     gpu_zero(r->st, sizeof(DecodeState));
     r->log = (TcmTop2 *)gpu_alloc(kLogCap * sizeof(TcmTop2));
-    const size_t part = (size_t)d->s.kvheads * (kAttnSplits + kMaxGroups) * kAttnPartialFloats;
-    r->attn_part = (float *)gpu_alloc(part * sizeof(float));
-    const size_t counters = (size_t)d->s.kvheads * (kMaxGroups + 1) * sizeof(unsigned);
-    r->attn_counters = (unsigned *)gpu_alloc(counters);
-    gpu_zero(r->attn_counters, counters);
+    r->attn_part = nullptr;  // the cluster combine keeps its partials in shared memory
+    r->attn_counters = nullptr;
     r->grid = sm_count();
     r->top_pv = (float *)gpu_alloc((size_t)2 * r->grid * sizeof(float));
     r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid * sizeof(int));
