@@ -691,7 +691,7 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Shape &s = r->d->s;
     const float *keys = r->b.keys + slot_offset(r, layer), *values = r->b.values + slot_offset(r, layer);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kCluster, s.kvheads);
+    cfg.gridDim = dim3(kCluster * kClustersPerHead, s.kvheads);
     cfg.blockDim = dim3(kDecodeAttnThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream();
@@ -705,8 +705,8 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
     TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6>, (const float *)r->b.q, keys, values, r->b.capacity,
-                                (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim), r->b.attention,
-                                trace_slot(r)));
+                                (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim), r->attn_part,
+                                r->attn_counters, r->b.attention, trace_slot(r)));
 }
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
     ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st, trace_slot(r)};
@@ -848,8 +848,9 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->st = (DecodeState *)gpu_alloc(sizeof(DecodeState));
     gpu_zero(r->st, sizeof(DecodeState));
     r->log = (TcmTop2 *)gpu_alloc(kLogCap * sizeof(TcmTop2));
-    r->attn_part = nullptr;  // the cluster combine keeps its partials in shared memory
-    r->attn_counters = nullptr;
+    r->attn_part = (float *)gpu_alloc((size_t)d->s.kvheads * kClustersPerHead * kAttnPartialFloats * sizeof(float));
+    r->attn_counters = (unsigned *)gpu_alloc((size_t)d->s.kvheads * sizeof(unsigned));
+    gpu_zero(r->attn_counters, (size_t)d->s.kvheads * sizeof(unsigned));
     r->grid = sm_count();
     r->top_pv = (float *)gpu_alloc((size_t)2 * r->grid * sizeof(float));
     r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid * sizeof(int));
