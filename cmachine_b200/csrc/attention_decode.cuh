@@ -115,7 +115,7 @@ constexpr int kClustersPerHead = 4;
 constexpr int kSingleClusterRows = 1024;  // caches up to this length use one cluster per head
 
 template <int G>
-__global__ void __launch_bounds__(kDecodeAttnThreads, 1) attn_decode_kernel(
+__global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
     const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
     float *__restrict__ out, unsigned long long *__restrict__ trace) {
