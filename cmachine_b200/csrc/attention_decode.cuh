@@ -132,13 +132,18 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
     if (mark && tid == 0) mark[0] = attn_clock();
-    pdl_wait();
-    if (mark && tid == 0) mark[1] = attn_clock();
-    pdl_trigger();
+    // The position is set before a token's first kernel and the cache rows
+    // below it were written by earlier tokens, so the row split and an L2
+    // prefetch of those rows need not wait for the q/k/v kernel; only q and the
+    // newest row (written by it) are read after griddepcontrol.wait.
     const int L = min(*position + 1, capacity);
     const int clusters = (int)(gridDim.x / kCluster);
     const bool multi = L > kSingleClusterRows && clusters > 1;
-    if (!multi && cid > 0) return;  // whole clusters leave together
+    if (!multi && cid > 0) {  // whole clusters leave together
+        pdl_wait();
+        pdl_trigger();
+        return;
+    }
     const int ctas = multi ? clusters * kCluster : kCluster, cta = multi ? cid * kCluster + rank : rank;
     const int chunk = (L + ctas - 1) / ctas;
     const int t0 = min(L, cta * chunk), t1 = min(L, t0 + chunk);
@@ -146,6 +151,14 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
     const float4 *kb = reinterpret_cast<const float4 *>(keys + (size_t)kvh * capacity * kHeadDim);
     const float4 *vb = reinterpret_cast<const float4 *>(values + (size_t)kvh * capacity * kHeadDim);
+    for (int t = r0 + (lane >> 2); t < min(r1, L - 1); t += 8) {
+        const int part = lane & 3;  // four 128-byte lines per 512-byte row
+        prefetch_l2(reinterpret_cast<const char *>(kb + (size_t)t * (kHeadDim / 4)) + 128 * part);
+        prefetch_l2(reinterpret_cast<const char *>(vb + (size_t)t * (kHeadDim / 4)) + 128 * part);
+    }
+    pdl_wait();
+    if (mark && tid == 0) mark[1] = attn_clock();
+    pdl_trigger();
 
     float4 q4[G], acc[G];
 #pragma unroll
