@@ -140,8 +140,8 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int clusters = (int)(gridDim.x / kCluster);
     const bool multi = L > kSingleClusterRows && clusters > 1;
     if (!multi && cid > 0) {  // whole clusters leave together
-        pdl_wait();
         pdl_trigger();
+        if (mark && tid == 0) mark[0] = 0ull;  // no work: not part of the timeline
         return;
     }
     const int ctas = multi ? clusters * kCluster : kCluster, cta = multi ? cid * kCluster + rank : rank;
