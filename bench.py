@@ -111,21 +111,25 @@ def dist_setup(n_gpus: int):
         import torch.distributed as dist
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
         return world, rank, local, dist, torch
     return 1, 0, local, None, None
 
 
 def barrier(dist, torch):
+    """All ranks meet; with NCCL the device is drained on both sides."""
     if dist:
         dist.barrier()
-        torch.cuda.synchronize()
+        if dist.get_backend() == "nccl":
+            torch.cuda.synchronize()
 
 
 def max_over_ranks(value: float, dist, torch) -> float:
+    """The largest value over all ranks (device time of the slowest rank)."""
     if not dist:
         return value
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -327,7 +331,7 @@ def main():
         print(json.dumps({
             "metric": METRIC, "impl": "reference", "value": round(rate, 4), "unit": "tokens/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16-weights/f32" if cfg["profile"] == 2 else "f32", "data": "synthetic",
             "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": cfg["layers"], "batch": 1},
             "cpu_baseline": {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
