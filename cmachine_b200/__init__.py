@@ -51,7 +51,8 @@ class SessionView(Structure):
                                      "dense_layers", "fused")] + [
         ("depth", ctypes.c_uint), ("session_id", c_uint64), ("epoch", c_uint64), ("lineage_id", c_uint64),
         ("checkpoint_serial", c_uint64), ("top_frame", c_uint64), ("top", Top2), ("keys", c_void_p),
-        ("values", c_void_p), ("x", c_void_p), ("logits", c_void_p), ("allocated_bytes", c_size_t)]
+        ("values", c_void_p), ("x", c_void_p), ("logits", c_void_p), ("allocated_bytes", c_size_t),
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("attention", c_void_p)]
 
 
 def qwen_shape(layers: int = 28, max_position: int = 32768) -> Shape:
@@ -63,6 +64,17 @@ def qwen_shape(layers: int = 28, max_position: int = 32768) -> Shape:
 # norms 1) and the parity tests' (nonzero biases, non-unit norms).
 BENCH_LAW = FillLaw(Fill(0.0, 0.02), Fill(1.0, 0.0), Fill(0.0, 0.0))
 TEST_LAW = FillLaw(Fill(0.0, 0.02), Fill(1.0, 0.1), Fill(0.0, 0.05))
+
+class RingView(Structure):
+    """QwenB200RingView (host/session_view.c): the bounded cache's state."""
+    _fields_ = [("cursor", c_int), ("population", c_uint64), ("rng", c_uint64)] + [
+        (n, c_int) for n in ("write_slot", "sample_slot", "active", "capacity", "transaction", "fused", "layers",
+                             "reservoir_count")] + [
+        (n, ctypes.c_ulonglong) for n in ("calls", "published", "restores", "main_tokens")] + [
+        (n, c_size_t) for n in ("arena_bytes", "gpu_bytes", "host_bytes")] + [
+        ("arena", c_void_p), ("positions", c_void_p), ("order", c_void_p), ("weights", c_void_p),
+        ("cut0_sample_position", c_int)]
+
 
 OBSERVER = ctypes.CFUNCTYPE(None, c_void_p, c_int, c_int, c_int, POINTER(c_float), c_size_t)
 PORT_NAMES = ["input", "query", "key", "value", "attention", "mlp_input", "mlp_gate", "mlp_up", "mlp_return",
@@ -101,6 +113,13 @@ def _declare(L, strict: bool = True):
         "gpu_encode_current": (c_int, [P, P, P, P, P, c_int, c_int, P]),
         "gpu_byte_attention": (None, [P, P, P, P, P, P, P, P, c_int, c_int]),
         "gpu_ring_attention": (None, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int]),
+        "gpu_attention_static": (c_int, [P, P, P, P, c_int, c_int, c_int, c_int, c_int]),
+        # include/bounded_cache.h
+        "ring_open": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int]),
+        "ring_begin": (c_int, [P, c_int]), "ring_abort": (c_int, [P]), "ring_finish": (c_int, [P]),
+        "ring_push": (c_int, [P, c_int]), "ring_mark": (c_int, [P, POINTER(c_uint64)]),
+        "ring_rollback": (c_int, [P, c_uint64]), "ring_commit": (c_int, [P, c_uint64]), "ring_close": (None, [P]),
+        "ring_step": (c_int, [P, c_int, c_int, P, P, P, P, P]),
         # include/qwen.h
         "qwen_model_init_seeded": (c_int, [P, POINTER(Shape), c_uint64, POINTER(FillLaw), c_int, c_int]),
         "qwen_model_free": (None, [P]),
@@ -113,6 +132,7 @@ def _declare(L, strict: bool = True):
         "qwen_stack_rollback": (c_int, [P, c_uint64]), "qwen_stack_commit": (c_int, [P, c_uint64]),
         "qwen_reset": (c_int, [P]), "qwen_port_name": (ctypes.c_char_p, [c_int]),
         "qwen_generate": (c_int, [P, c_int, POINTER(c_int)]),
+        "qwen_complete_token": (c_int, [P]),
         # include/qwen_b200.h
         "qwen_b200_decoder_weight_bytes": (c_size_t, [P]),
         "qwen_b200_launches_per_token": (c_int, [P]),
@@ -127,6 +147,8 @@ def _declare(L, strict: bool = True):
         "qwen_b200_set_device": (None, [c_int]), "qwen_b200_sm_count": (c_int, []),
         "qwen_b200_seeded_fill": (None, [P, c_int, c_uint64, c_uint32, c_size_t, c_float, c_float]),
         "qwen_b200_register_matrix": (None, [P, c_int, c_int, c_int]),
+        "qwen_b200_complete": (c_int, [P, POINTER(Top2)]), "qwen_b200_can_complete": (c_int, [P]),
+        "qwen_b200_ring_rows": (None, [P, c_int, c_int, P, c_int, c_int, c_int]),
         "qwen_b200_unregister_matrix": (None, [P]),
         # host/session_view.c
         "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),
@@ -136,6 +158,8 @@ def _declare(L, strict: bool = True):
         "qwen_b200_session_observe": (None, [P, OBSERVER, P, c_int, c_int]),
         "qwen_b200_model_weight_bytes": (c_size_t, [P]), "qwen_b200_model_decoder": (P, [P]),
         "qwen_b200_session_runner": (P, [P]),
+        "qwen_b200_ring_size": (c_size_t, []), "qwen_b200_ring_view": (None, [P, POINTER(RingView)]),
+        "qwen_b200_ring_fail": (None, [P, c_int, c_int]),
     }
     for name, (res, args) in sig.items():
         try:
@@ -292,10 +316,92 @@ class Session:
                 self.L.gpu_read(ptr(out[h]), c_void_p(base + h * v.capacity * s.head * 4), v.position * s.head * 4)
         return out
 
+    def kv_rows(self):
+        """This token's K and V rows of the last layer computed: ([kvheads * head], [kvheads * head])."""
+        v, s = self.view(), self.model.shape
+        k, vv = np.empty(s.kvheads * s.head, np.float32), np.empty(s.kvheads * s.head, np.float32)
+        self.L.gpu_read(ptr(k), c_void_p(v.k), k.nbytes)
+        self.L.gpu_read(ptr(vv), c_void_p(v.v), vv.nbytes)
+        return k, vv
+
+    def complete_token(self) -> int: return self.L.qwen_complete_token(self.handle)
+
     @property
     def runner(self): return self.L.qwen_b200_session_runner(self.handle)
 
     def free(self):
         if self._live:
             self.L.qwen_session_free(self.handle)
+            self._live = False
+
+
+class Ring:
+    """A bounded anchors/recent/reservoir byte-codec cache over its own session
+    (include/bounded_cache.h); methods return the C entry point's status code."""
+
+    def __init__(self, model: Model, logical: int, anchors: int, recent: int, sample: int, full: int = 0):
+        L = self.L = model.L
+        self.model = model
+        self.session = Session.__new__(Session)
+        self.session.L, self.session.model = L, model
+        self.session._buf = ctypes.create_string_buffer(L.qwen_b200_session_size())
+        self.session.handle = ctypes.cast(self.session._buf, c_void_p)
+        self.session._callbacks, self.session._observer = (None, None), None
+        self._buf = ctypes.create_string_buffer(L.qwen_b200_ring_size())
+        self.handle = ctypes.cast(self._buf, c_void_p)
+        if L.ring_open(self.handle, self.session.handle, model.handle, logical, anchors, recent, sample, full):
+            raise ValueError("ring_open refused the sizes or the model")
+        self.session._live = True
+        self._live = True
+
+    def push(self, token: int) -> int: return self.L.ring_push(self.handle, token)
+    def begin(self, token: int) -> int: return self.L.ring_begin(self.handle, token)
+    def abort(self) -> int: return self.L.ring_abort(self.handle)
+    def finish(self) -> int: return self.L.ring_finish(self.handle)
+    def advance_layer(self) -> int: return self.session.advance_layer()
+
+    def mark(self):
+        frame = c_uint64(0)
+        return self.L.ring_mark(self.handle, ctypes.byref(frame)), frame.value
+
+    def rollback(self, frame: int) -> int: return self.L.ring_rollback(self.handle, frame)
+    def commit(self, frame: int) -> int: return self.L.ring_commit(self.handle, frame)
+    def fail(self, layer: int, position: int): self.L.qwen_b200_ring_fail(self.handle, layer, position)
+
+    def reset(self) -> int:
+        """The bounded serve's reset: qwen_reset, then zero logits (src/qwen_bounded_serve.c:58)."""
+        e = self.session.reset()
+        if not e:
+            self.L.gpu_zero(c_void_p(self.session.view().logits), self.model.shape.vocab * 4)
+        return e
+
+    def view(self) -> RingView:
+        v = RingView()
+        self.L.qwen_b200_ring_view(self.handle, ctypes.byref(v))
+        return v
+
+    def positions(self) -> np.ndarray:
+        v = self.view()
+        return np.ctypeslib.as_array(ctypes.cast(v.positions, POINTER(c_int)), (v.capacity,)).copy()
+
+    def order(self):
+        v = self.view()
+        if not v.active:
+            return np.zeros(0, np.int32), np.zeros(0, np.float32)
+        o = np.ctypeslib.as_array(ctypes.cast(v.order, POINTER(c_int)), (v.active,)).copy()
+        w = np.ctypeslib.as_array(ctypes.cast(v.weights, POINTER(c_float)), (v.active,)).copy()
+        return o, w
+
+    def arena(self) -> np.ndarray:
+        v = self.view()
+        out = np.empty(v.arena_bytes, np.uint8)
+        self.L.gpu_read(ptr(out), c_void_p(v.arena), v.arena_bytes)
+        return out
+
+    def logits(self) -> np.ndarray: return self.session.logits()
+
+    def close(self):
+        if self._live:
+            self.L.ring_close(self.handle)
+            self.session.free()
             self._live = False

@@ -21,6 +21,7 @@
 #pragma once
 #include "common.cuh"
 #include "attention.cuh"
+#include "../../include/qwen_b200.h"
 #include <cooperative_groups.h>
 
 namespace tcm {
@@ -114,11 +115,143 @@ __device__ __forceinline__ void cta_merge(const float (&m)[G], const float (&l)[
 constexpr int kClustersPerHead = 4;
 constexpr int kSingleClusterRows = 1024;  // caches up to this length use one cluster per head
 
-template <int G>
+// ---------------------------------------------------------------- row sources
+// The kernel reads rows through a source: rows t in [0, length()) of the KV
+// head bound with bind(); load() gives the lane's four dimensions of K and V
+// (FP32), bias() an additive score term, prefetch_line() warms one 128-byte
+// line of row t in L2. current() runs after the dependency wait, before the
+// first load.
+
+// Dense FP32 rows [kvheads][capacity][128]; rows 0..position.
+struct DenseRows {
+    static constexpr bool kBias = false;
+    static constexpr int kLines = 4;  // 128-byte lines per row and kind
+    const float *keys, *values;
+    int capacity;
+    const int *position;
+    const float4 *kb, *vb;
+    __device__ __forceinline__ void bind(int kvh) {
+        kb = reinterpret_cast<const float4 *>(keys + (size_t)kvh * capacity * kHeadDim);
+        vb = reinterpret_cast<const float4 *>(values + (size_t)kvh * capacity * kHeadDim);
+    }
+    __device__ __forceinline__ int length() const { return min(*position + 1, capacity); }
+    // The newest row is written by the q/k/v kernel of this token: not prefetched.
+    __device__ __forceinline__ int prefetch_limit() const { return length() - 1; }
+    __device__ __forceinline__ void prefetch_line(int t, int part) const {
+        prefetch_l2(reinterpret_cast<const char *>(kb + (size_t)t * (kHeadDim / 4)) + 128 * part);
+        prefetch_l2(reinterpret_cast<const char *>(vb + (size_t)t * (kHeadDim / 4)) + 128 * part);
+    }
+    __device__ __forceinline__ void current(int, int, int) {}
+    __device__ __forceinline__ void load(int t, int lane, float4 &k, float4 &v) const {
+        k = __ldcg(kb + (size_t)t * (kHeadDim / 4) + lane);
+        v = __ldcg(vb + (size_t)t * (kHeadDim / 4) + lane);
+    }
+    __device__ __forceinline__ float bias(int) const { return 0.f; }
+};
+
+// One (kind, KV head) row of the byte codec (src/qwen_cache.inc:3-15): s =
+// max|x| / 127 (1 for a zero row), code = clamp(roundf(x / s), +-127), with
+// IEEE division as the reference's encode_current; non-finite elements encode
+// as 0 and flag the row. When `codes` is set the warp stores the row and its
+// scale (unless the scale itself is unusable) and raises bit 2 of *invalid on
+// a non-finite row. Returns the lane's dequantised dimensions (float)code * s.
+__device__ __forceinline__ float4 encode_row(const float4 x, int lane, unsigned *codes, float *scale_out, int *invalid) {
+    auto fin_abs = [](float v) { return isfinite(v) ? fabsf(v) : 0.f; };
+    const bool fin = isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w);
+    const float m = warp_max(fmaxf(fmaxf(fin_abs(x.x), fin_abs(x.y)), fmaxf(fin_abs(x.z), fin_abs(x.w))));
+    const bool all_fin = __all_sync(0xffffffffu, fin);
+    const float s = m > 0.f ? __fdiv_rn(m, 127.f) : 1.f;
+    const bool ok = s > 0.f && isfinite(s);
+    auto code = [&](float v) {
+        float c = isfinite(v) ? roundf(__fdiv_rn(v, s)) : 0.f;
+        return (int)fminf(127.f, fmaxf(-127.f, c));
+    };
+    const int c0 = code(x.x), c1 = code(x.y), c2 = code(x.z), c3 = code(x.w);
+    if (codes) {
+        if (ok) {
+            codes[lane] = (unsigned)(c0 & 0xff) | ((unsigned)(c1 & 0xff) << 8) | ((unsigned)(c2 & 0xff) << 16) |
+                          ((unsigned)(c3 & 0xff) << 24);
+            if (lane == 0) *scale_out = s;
+        }
+        if (lane == 0 && (!all_fin || !ok)) atomicOr(invalid, 2);
+    }
+    return make_float4(__fmul_rn((float)c0, s), __fmul_rn((float)c1, s), __fmul_rn((float)c2, s), __fmul_rn((float)c3, s));
+}
+__device__ __forceinline__ float4 dequant4(unsigned w, float s) {
+    return make_float4(__fmul_rn((float)(signed char)(w & 0xffu), s), __fmul_rn((float)(signed char)((w >> 8) & 0xffu), s),
+                       __fmul_rn((float)(signed char)((w >> 16) & 0xffu), s), __fmul_rn((float)(signed char)(w >> 24), s));
+}
+
+// Ring rows of one layer's byte-codec arena (per layer K codes [2][rows][128],
+// V codes [2][rows][128], scales [kind * 2 + head][rows]). Logical rows are the
+// retained anchor slots, then the retained reservoir slots, then the retained
+// recent slots; the softmax does not depend on the order. The write slot's row
+// is this token's K/V: every warp encodes it from the FP32 rows in registers
+// (identical bits everywhere), and CTA 0 of the head also stores it.
+struct ByteRows {
+    static constexpr bool kBias = true;
+    static constexpr int kLines = 1;
+    const signed char *arena;  // this layer
+    int rows, anchors, reservoir_base;  // reservoir_base = anchors + recent
+    const QwenB200RingStep *step;
+    const float *kcur, *vcur;           // this token's K, V rows [2][128] (FP32)
+    int *invalid;
+    // bound per CTA
+    const unsigned *kc, *vc;
+    const float *ks, *vs;
+    int na, nm, nr, write_slot, kvh;
+    bool weighted;
+    float bias_v;
+    float4 kq, vq;
+    __device__ __forceinline__ void bind(int h) {
+        kvh = h;
+        kc = reinterpret_cast<const unsigned *>(arena + (size_t)h * rows * kHeadDim);
+        vc = reinterpret_cast<const unsigned *>(arena + (size_t)rows * 2 * kHeadDim + (size_t)h * rows * kHeadDim);
+        ks = reinterpret_cast<const float *>(arena + (size_t)rows * 4 * kHeadDim) + (size_t)h * rows;
+        vs = reinterpret_cast<const float *>(arena + (size_t)rows * 4 * kHeadDim) + (size_t)(2 + h) * rows;
+        na = step->anchors_n;
+        nm = step->reservoir_n;
+        nr = step->recent_n;
+        write_slot = step->write_slot;
+        weighted = step->weighted != 0;
+        bias_v = step->bias;
+    }
+    __device__ __forceinline__ int length() const { return na + nm + nr; }
+    __device__ __forceinline__ int prefetch_limit() const { return length(); }
+    __device__ __forceinline__ int slot(int t) const {
+        return t < na ? t : (t < na + nm ? reservoir_base + (t - na) : anchors + (t - na - nm));
+    }
+    __device__ __forceinline__ void prefetch_line(int t, int) const {
+        const int s = slot(t);
+        prefetch_l2(kc + (size_t)s * (kHeadDim / 4));
+        prefetch_l2(vc + (size_t)s * (kHeadDim / 4));
+    }
+    __device__ __forceinline__ void current(int lane, int warp, int cta) {
+        const float4 kx = reinterpret_cast<const float4 *>(kcur + (size_t)kvh * kHeadDim)[lane];
+        const float4 vx = reinterpret_cast<const float4 *>(vcur + (size_t)kvh * kHeadDim)[lane];
+        const bool store = cta == 0 && warp == 0;
+        unsigned *kd = store ? const_cast<unsigned *>(kc) + (size_t)write_slot * (kHeadDim / 4) : nullptr;
+        unsigned *vd = store ? const_cast<unsigned *>(vc) + (size_t)write_slot * (kHeadDim / 4) : nullptr;
+        kq = encode_row(kx, lane, kd, const_cast<float *>(ks) + write_slot, invalid);
+        vq = encode_row(vx, lane, vd, const_cast<float *>(vs) + write_slot, invalid);
+    }
+    __device__ __forceinline__ void load(int t, int lane, float4 &k, float4 &v) const {
+        const int s = slot(t);
+        if (s == write_slot) {
+            k = kq;
+            v = vq;
+            return;
+        }
+        k = dequant4(__ldcg(kc + (size_t)s * (kHeadDim / 4) + lane), __ldcg(ks + s));
+        v = dequant4(__ldcg(vc + (size_t)s * (kHeadDim / 4) + lane), __ldcg(vs + s));
+    }
+    __device__ __forceinline__ float bias(int t) const { return (weighted && t >= na && t < na + nm) ? bias_v : 0.f; }
+};
+
+template <int G, class Rows>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
-    const float *__restrict__ q, const float *__restrict__ keys, const float *__restrict__ values, int capacity,
-    const int *__restrict__ position, float inv_sqrt_dim, float *__restrict__ part, unsigned *__restrict__ counters,
-    float *__restrict__ out, unsigned long long *__restrict__ trace) {
+    Rows rows, const float *__restrict__ q, float inv_sqrt_dim, float *__restrict__ part,
+    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace) {
     static_assert(G <= 8, "query heads per KV head are padded to eight");
     constexpr int GP = 8;       // padded heads: 4 rows x 8 heads = 32 scores, one per lane
     constexpr int kStep = 4;    // rows per step
@@ -132,11 +265,13 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
     if (mark && tid == 0) mark[0] = attn_clock();
-    // The position is set before a token's first kernel and the cache rows
-    // below it were written by earlier tokens, so the row split and an L2
-    // prefetch of those rows need not wait for the q/k/v kernel; only q and the
-    // newest row (written by it) are read after griddepcontrol.wait.
-    const int L = min(*position + 1, capacity);
+    // The token state (position, ring step) is written before a token's first
+    // kernel and the cache rows below the newest were written by earlier
+    // tokens, so the row split and an L2 prefetch of those rows need not wait
+    // for the q/k/v kernel; q and this token's K/V are read after
+    // griddepcontrol.wait.
+    rows.bind(kvh);
+    const int L = rows.length();
     const int clusters = (int)(gridDim.x / kCluster);
     const bool multi = L > kSingleClusterRows && clusters > 1;
     if (!multi && cid > 0) {  // whole clusters leave together
@@ -149,16 +284,15 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int t0 = min(L, cta * chunk), t1 = min(L, t0 + chunk);
     const int per_warp = (t1 - t0 + kDecodeAttnWarps - 1) / kDecodeAttnWarps;
     const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
-    const float4 *kb = reinterpret_cast<const float4 *>(keys + (size_t)kvh * capacity * kHeadDim);
-    const float4 *vb = reinterpret_cast<const float4 *>(values + (size_t)kvh * capacity * kHeadDim);
-    for (int t = r0 + (lane >> 2); t < min(r1, L - 1); t += 8) {
-        const int part = lane & 3;  // four 128-byte lines per 512-byte row
-        prefetch_l2(reinterpret_cast<const char *>(kb + (size_t)t * (kHeadDim / 4)) + 128 * part);
-        prefetch_l2(reinterpret_cast<const char *>(vb + (size_t)t * (kHeadDim / 4)) + 128 * part);
+    {
+        constexpr int kRowsPerPass = 32 / Rows::kLines;
+        const int limit = min(r1, rows.prefetch_limit());
+        for (int t = r0 + lane / Rows::kLines; t < limit; t += kRowsPerPass) rows.prefetch_line(t, lane % Rows::kLines);
     }
     pdl_wait();
     if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
+    rows.current(lane, warp, cta);
 
     float4 q4[G], acc[G];
 #pragma unroll
@@ -174,9 +308,12 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     auto load_rows = [&](int t, float4 (&kk)[kStep], float4 (&vv)[kStep]) {
 #pragma unroll
         for (int i = 0; i < kStep; i++) {
-            const bool ok = t + i < r1;
-            kk[i] = ok ? __ldcg(kb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-            vv[i] = ok ? __ldcg(vb + (size_t)(t + i) * (kHeadDim / 4) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t + i < r1) {
+                rows.load(t + i, lane, kk[i], vv[i]);
+            } else {
+                kk[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
     };
     if (r0 < r1) load_rows(r0, k4, v4);
@@ -211,7 +348,14 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
             }
         }
         const bool valid = t + my_row < r1 && my_head < G;
-        const float sc = valid ? v[0] * inv_sqrt_dim : -INFINITY;
+        float sc;
+        if constexpr (Rows::kBias) {
+            // (score + bias) / sqrt(128): the reference adds the bias before
+            // the softmax scales (src/qwen_cache.inc:34, src/qwen_cuda.cu:67).
+            sc = valid ? __fmul_rn(__fadd_rn(v[0], rows.bias(t + my_row)), inv_sqrt_dim) : -INFINITY;
+        } else {
+            sc = valid ? v[0] * inv_sqrt_dim : -INFINITY;
+        }
         float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m_run, mx);

@@ -26,13 +26,17 @@ namespace tcm {
 // the readout's last CTA publishes the top-2 and, for chained greedy decode,
 // feeds top-1 back as the next token and advances the position. `fault`
 // collects the bits of any pipeline wait that ran out.
+// Bits of `invalid`: 1 non-finite logits, 2 a non-finite K/V row encoded into
+// a ring arena. `ring` is the token's ring bookkeeping (ring layers only).
 struct DecodeState {
     int token, position, step, invalid;
     unsigned fault;
     int pad[3];
     TcmTop2 top;
+    QwenB200RingStep ring;
 };
 constexpr int kLogCap = 4096;
+constexpr int kRingRowBytes = 528;  // one ring row: 4 x 128 codes + 4 FP32 scales
 
 namespace {
 
@@ -578,6 +582,57 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     }
 }
 
+// ---------------------------------------------------------------- ring token cut
+// One CTA per layer moves the 528-byte rows of the write and sample slots
+// between the arena and the save area (132 words a row: 4 code segments of 32
+// words, then 4 scales); every CTA copies a share of the logits. Mode 0 saves
+// both rows, then copies the saved write row into the sample slot (the
+// reference's per-layer ring_copy_row, src/bounded_cache.h:38-46, done for all
+// layers at the start of the token); mode 1 writes both saved rows back.
+constexpr int kRingRowWords = 132;
+__device__ __forceinline__ unsigned *ring_word(unsigned char *layer, int rows, int slot, int w) {
+    if (w < 128) {
+        const int seg = w >> 5, kind = seg >> 1, head = seg & 1;
+        return reinterpret_cast<unsigned *>(layer + (size_t)kind * rows * 256 + ((size_t)head * rows + slot) * 128) + (w & 31);
+    }
+    const int j = w - 128;  // kind * 2 + head
+    return reinterpret_cast<unsigned *>(layer + (size_t)rows * 512) + (size_t)j * rows + slot;
+}
+struct RingCutArgs {
+    unsigned char *arena, *save;
+    const float *logits;
+    float *logits_save;
+    const DecodeState *st;  // slots from the token state when set
+    int rows, layers, vocab, write_slot, sample_slot, mode;
+};
+__global__ void __launch_bounds__(256) ring_cut_kernel(RingCutArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int ws = a.st ? a.st->ring.write_slot : a.write_slot, ss = a.st ? a.st->ring.sample_slot : a.sample_slot;
+    const int l = blockIdx.x, w = threadIdx.x;
+    if (l < a.layers && w < kRingRowWords) {
+        unsigned char *layer = a.arena + (size_t)l * a.rows * kRingRowBytes;
+        unsigned *sw = reinterpret_cast<unsigned *>(a.save + (size_t)l * 2 * kRingRowBytes) + w;
+        unsigned *aw = ring_word(layer, a.rows, ws, w);
+        if (a.mode == 0) {
+            const unsigned old_write = *aw;
+            sw[0] = old_write;
+            if (ss >= 0) {
+                unsigned *as = ring_word(layer, a.rows, ss, w);
+                sw[kRingRowWords] = *as;
+                *as = old_write;
+            }
+        } else {
+            *aw = sw[0];
+            if (ss >= 0) *ring_word(layer, a.rows, ss, w) = sw[kRingRowWords];
+        }
+    }
+    if (a.logits_save) {
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.vocab; i += gridDim.x * blockDim.x)
+            a.logits_save[i] = a.logits[i];
+    }
+}
+
 // Token state from kernel arguments: nothing in host memory is read after the
 // launch call returns, so chained enqueues never race a host buffer.
 __global__ void set_state_kernel(DecodeState *st, int token, int position) {
@@ -635,12 +690,16 @@ struct QwenB200Runner {
     unsigned long long *trace;  // timeline buffer (kTraceLaunches x kTraceCtas x 4) or null
     int trace_next;
     int grid, launches;
+    bool ring_on;               // cache-callback layers are served by `ring`
+    QwenB200Ring ring;
+    QwenB200RingStep staged;    // written with the next token state
 };
 
 namespace {
 
 void setup_attention() {
-    TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6, DenseRows>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6, ByteRows>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
 }
 template <typename WT> void setup_kernels_typed() {
     set_smem(qkv_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
@@ -687,9 +746,9 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.trace = trace_slot(r);
     launch(qkv_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
 }
-void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
+template <class Rows>
+void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl) {
     const QwenB200Shape &s = r->d->s;
-    const float *keys = r->b.keys + slot_offset(r, layer), *values = r->b.values + slot_offset(r, layer);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCluster * kClustersPerHead, s.kvheads);
     cfg.blockDim = dim3(kDecodeAttnThreads);
@@ -704,9 +763,37 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6>, (const float *)r->b.q, keys, values, r->b.capacity,
-                                (const int *)&r->st->position, 1.0f / sqrtf((float)kHeadDim), r->attn_part,
-                                r->attn_counters, r->b.attention, trace_slot(r)));
+    TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6, Rows>, rows, q, 1.0f / sqrtf((float)kHeadDim),
+                                r->attn_part, r->attn_counters, out, trace_slot(r)));
+}
+void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
+    DenseRows rows = {};
+    rows.keys = r->b.keys + slot_offset(r, layer);
+    rows.values = r->b.values + slot_offset(r, layer);
+    rows.capacity = r->b.capacity;
+    rows.position = &r->st->position;
+    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl);
+}
+void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const float *k, const float *v, float *out,
+                           bool pdl) {
+    const QwenB200Ring &g = r->ring;
+    ByteRows rows = {};
+    rows.arena = (const signed char *)g.arena + (size_t)layer * g.rows * kRingRowBytes;
+    rows.rows = g.rows;
+    rows.anchors = g.anchors;
+    rows.reservoir_base = g.anchors + g.recent;
+    rows.step = &r->st->ring;
+    rows.kcur = k;
+    rows.vcur = v;
+    rows.invalid = &r->st->invalid;
+    launch_attention_rows(r, rows, q, out, pdl);
+}
+void launch_ring_cut(QwenB200Runner *r, const DecodeState *st, int write_slot, int sample_slot, int mode, bool logits,
+                     bool pdl) {
+    const QwenB200Ring &g = r->ring;
+    RingCutArgs a = {(unsigned char *)g.arena, (unsigned char *)g.save, r->b.logits, logits ? g.logits_save : nullptr,
+                     st, g.rows, r->d->s.layers, r->d->s.vocab, write_slot, sample_slot, mode};
+    launch(ring_cut_kernel, dim3(r->grid), dim3(256), 0, stream(), pdl, a);
 }
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
     ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st, trace_slot(r)};
@@ -738,7 +825,8 @@ template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
 void launch_layer(QwenB200Runner *r, int layer, bool pdl_first) {
     if (r->d->dtype == 2) launch_qkv<uint16_t>(r, layer, pdl_first);
     else launch_qkv<float>(r, layer, pdl_first);
-    launch_attention(r, layer, true);
+    if (has_dense(r, layer)) launch_attention(r, layer, true);
+    else launch_ring_attention(r, layer, r->b.q, r->b.k, r->b.v, r->b.attention, true);
     if (r->d->dtype == 2) launch_mlp<uint16_t>(r, layer, true);
     else launch_mlp<float>(r, layer, true);
 }
@@ -756,10 +844,12 @@ bool all_dense(const QwenB200Runner *r) {
         if (s < 0) return false;
     return true;
 }
+// Every layer has a fused attention: a dense slot, or the attached ring.
+bool all_served(const QwenB200Runner *r) { return r->ring_on || all_dense(r); }
 
 int ensure_graph(QwenB200Runner *r) {
     if (r->graph_ready) return 0;
-    if (!all_dense(r)) return -1;
+    if (!all_served(r)) return -1;
     cudaStream_t s = stream();
     cudaGraph_t g;
     TCM_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
@@ -777,8 +867,20 @@ void write_state(QwenB200Runner *r, int token, int position) {
     r->host->step = 0;
     r->host->invalid = 0;
     r->host->fault = 0u;
-    TCM_CUDA(cudaMemcpyAsync(r->st, r->host, 8 * sizeof(int), cudaMemcpyHostToDevice, stream()));
+    r->host->ring = r->staged;
+    // With a ring the whole state goes (the step follows the top-2 field).
+    const size_t bytes = r->ring_on ? sizeof(DecodeState) : 8 * sizeof(int);
+    TCM_CUDA(cudaMemcpyAsync(r->st, r->host, bytes, cudaMemcpyHostToDevice, stream()));
     r->after_host = true;
+}
+// Opens a token: the state, and with a ring the token cut (row store, sample
+// copy, logits) before any layer.
+void start_token(QwenB200Runner *r, int token, int position) {
+    write_state(r, token, position);
+    if (r->ring_on) {
+        launch_ring_cut(r, r->st, 0, 0, 0, true, false);
+        r->after_host = false;
+    }
 }
 int read_top(QwenB200Runner *r, TcmTop2 *top) {
     TCM_CUDA(cudaMemcpyAsync(r->host, r->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream()));
@@ -788,10 +890,12 @@ int read_top(QwenB200Runner *r, TcmTop2 *top) {
         fprintf(stderr, "B200 decode: a pipeline wait ran out (fault bits 0x%x)\n", r->host->fault);
         return -4;
     }
+    if (r->host->invalid & 2) return -5;  // a ring layer encoded a non-finite row: the token aborts first
     return r->host->invalid ? -3 : 0;
 }
 bool valid_token(const QwenB200Runner *r, int token, int position) {
-    return token >= 0 && token < r->d->s.vocab && position >= 0 && position < r->b.capacity;
+    const int limit = r->ring_on ? r->ring.positions : r->b.capacity;
+    return token >= 0 && token < r->d->s.vocab && position >= 0 && position < limit;
 }
 
 cudaEvent_t g_marks[64][16];
@@ -881,7 +985,7 @@ void qwen_b200_runner_free(QwenB200Runner *r) {
 
 int qwen_b200_begin(QwenB200Runner *r, int token, int position) {
     if (!r || !valid_token(r, token, position)) return -1;
-    write_state(r, token, position);
+    start_token(r, token, position);
     return 0;
 }
 
@@ -920,13 +1024,72 @@ int qwen_b200_finish(QwenB200Runner *r, TcmTop2 *top) {
 
 int qwen_b200_token(QwenB200Runner *r, int token, int position, TcmTop2 *top) {
     if (!r || !valid_token(r, token, position) || ensure_graph(r)) return -1;
-    write_state(r, token, position);
+    start_token(r, token, position);
     TCM_CUDA(cudaGraphLaunch(r->graph, stream()));
-    return read_top(r, top);  // leaves after_host set by write_state
+    r->after_host = true;
+    return read_top(r, top);
+}
+
+int qwen_b200_complete(QwenB200Runner *r, TcmTop2 *top) {
+    if (!r || ensure_graph(r)) return -1;
+    TCM_CUDA(cudaGraphLaunch(r->graph, stream()));
+    r->after_host = true;
+    return read_top(r, top);
+}
+
+int qwen_b200_can_complete(const QwenB200Runner *r) { return r && all_served(r) ? 1 : 0; }
+
+int qwen_b200_ring_attach(QwenB200Runner *r, const QwenB200Ring *g) {
+    if (!r || !g || r->d->s.kvheads != 2 || g->rows < 1 || g->anchors < 0 || g->recent < 1 || g->reservoir < 0 ||
+        g->anchors + g->recent + g->reservoir != g->rows || !g->arena || !g->save || !g->logits_save ||
+        g->positions < 1 || g->positions > r->d->s.max_position || ((uintptr_t)g->arena & 15))
+        return -1;
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    if (r->graph_ready) {
+        TCM_CUDA(cudaGraphExecDestroy(r->graph));
+        r->graph_ready = false;
+    }
+    r->ring = *g;
+    r->ring_on = true;
+    r->staged = QwenB200RingStep{};
+    r->staged.sample_slot = -1;
+    r->launches = r->d->s.layers * 5 + 2;  // + the token cut
+    return 0;
+}
+
+int qwen_b200_ring_stage(QwenB200Runner *r, const QwenB200RingStep *step) {
+    if (!r || !r->ring_on || !step) return -1;
+    const QwenB200Ring &g = r->ring;
+    const QwenB200RingStep &t = *step;
+    const bool ok = t.write_slot >= 0 && t.write_slot < g.anchors + g.recent &&
+                    (t.sample_slot == -1 || (t.sample_slot >= g.anchors + g.recent && t.sample_slot < g.rows)) &&
+                    t.anchors_n >= 0 && t.anchors_n <= g.anchors && t.recent_n >= 0 && t.recent_n <= g.recent &&
+                    t.reservoir_n >= 0 && t.reservoir_n <= g.reservoir && t.anchors_n + t.reservoir_n + t.recent_n >= 1;
+    if (!ok) return -1;
+    r->staged = t;
+    return 0;
+}
+
+int qwen_b200_ring_attention(QwenB200Runner *r, int layer, const float *q, const float *k, const float *v, float *out) {
+    if (!r || !r->ring_on || layer < 0 || layer >= r->d->s.layers || has_dense(r, layer) || !q || !k || !v || !out)
+        return -1;
+    launch_ring_attention(r, layer, q, k, v, out, !r->after_host);
+    r->after_host = false;
+    return 0;
+}
+
+int qwen_b200_ring_status(QwenB200Runner *r) {
+    if (!r) return -1;
+    int invalid = 0;
+    TCM_CUDA(cudaMemcpyAsync(&r->host->invalid, &r->st->invalid, sizeof(int), cudaMemcpyDeviceToHost, stream()));
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    invalid = r->host->invalid;
+    r->after_host = true;
+    return (invalid & 2) ? -1 : 0;
 }
 
 int qwen_b200_enqueue(QwenB200Runner *r, int token, int position, int n) {
-    if (!r || n < 1 || n > kLogCap || !valid_token(r, token, position) || position + n > r->b.capacity ||
+    if (!r || r->ring_on || n < 1 || n > kLogCap || !valid_token(r, token, position) || position + n > r->b.capacity ||
         ensure_graph(r))
         return -1;
     set_state_kernel<<<1, 1, 0, stream()>>>(r->st, token, position);
@@ -1014,6 +1177,18 @@ float qwen_b200_time_stage(QwenB200Runner *r, int stage, int layer, int position
     TCM_CUDA(cudaEventDestroy(b));
     r->after_host = true;
     return total / reps;
+}
+
+void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int write_slot, int sample_slot, int mode) {
+    if (!arena || !save || rows < 1 || layers < 1 || layers > 64 || write_slot < 0 || write_slot >= rows ||
+        sample_slot < -1 || sample_slot >= rows || (mode != 0 && mode != 1)) {
+        fprintf(stderr, "qwen_b200_ring_rows: invalid arguments\n");
+        exit(2);
+    }
+    RingCutArgs a = {(unsigned char *)arena, (unsigned char *)save, nullptr, nullptr, nullptr, rows, layers, 0,
+                     write_slot, sample_slot, mode};
+    ring_cut_kernel<<<layers, 256, 0, stream()>>>(a);
+    TCM_CUDA(cudaGetLastError());
 }
 
 void qwen_b200_mark(int index) {

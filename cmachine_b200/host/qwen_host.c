@@ -319,6 +319,27 @@ int qwen_finish_token(QwenSession *s) {
     return 0;
 }
 
+int qwen_complete_token(QwenSession *s) {
+    const QwenModel *m = s->model;
+    if (s->phase != 2 || s->layer != 0) return -1;
+    const int observed = s->observer && s->observe_position == s->position;
+    if (!s->runner || observed || !qwen_b200_can_complete(s->runner)) {
+        while (s->layer < m->layers) {
+            int error = qwen_advance_layer(s);
+            if (error) return error;
+        }
+        return qwen_finish_token(s);
+    }
+    int status = qwen_b200_complete(s->runner, &s->top);
+    if (status == -3) { fprintf(stderr, "non-finite Qwen logits\n"); exit(2); }
+    if (status == -5) return -81;
+    uint64_t lineage;
+    if (status || take_id(&next_lineage_id, &lineage)) return -1;
+    s->layer = m->layers;
+    finish_bookkeeping(s, lineage);
+    return 0;
+}
+
 /* The whole token is one fused graph when no port is observed at this
  * position and every layer keeps its K/V in the session. */
 static int fused_token_ok(const QwenSession *s) {

@@ -11,6 +11,7 @@ typedef struct {
     TcmTop2 top;
     float *keys, *values, *x, *logits;
     size_t allocated_bytes;
+    float *q, *k, *v, *attention;
 } QwenSessionView;
 
 size_t qwen_b200_model_size(void) { return sizeof(QwenModel); }
@@ -25,6 +26,7 @@ void qwen_b200_session_view(const QwenSession *s, QwenSessionView *v) {
     v->checkpoint_serial = s->checkpoint_serial; v->top_frame = s->depth ? s->frames[s->depth - 1].id : 0;
     v->top = s->top; v->keys = s->keys; v->values = s->values; v->x = s->x; v->logits = s->logits;
     v->allocated_bytes = s->allocated_bytes;
+    v->q = s->q; v->k = s->k; v->v = s->v; v->attention = s->attention;
 }
 
 void qwen_b200_session_set_delivered(QwenSession *s, int delivered) { s->delivered = delivered; }
@@ -41,3 +43,35 @@ void qwen_b200_session_cache_guard(QwenSession *s, QwenCacheGuard guard) { s->ca
 size_t qwen_b200_model_weight_bytes(const QwenModel *m) { return m->weight_bytes; }
 const QwenB200Decoder *qwen_b200_model_decoder(const QwenModel *m) { return m->fused; }
 QwenB200Runner *qwen_b200_session_runner(const QwenSession *s) { return s->runner; }
+
+/* The bounded cache (include/bounded_cache.h), flattened. */
+#include "../../include/bounded_cache.h"
+typedef struct {
+    int cursor;
+    uint64_t population, rng;
+    int write_slot, sample_slot, active, capacity, transaction, fused, layers, reservoir_count;
+    unsigned long long calls, published, restores, main_tokens;
+    size_t arena_bytes, gpu_bytes, host_bytes;
+    void *arena;
+    int *positions, *order;
+    float *weights;
+    int cut0_sample_position;  /* cuts[0].positions[sample_slot] (the slot's pre-token position), or -2 */
+} QwenB200RingView;
+
+size_t qwen_b200_ring_size(void) { return sizeof(Ring); }
+
+void qwen_b200_ring_view(const Ring *c, QwenB200RingView *v) {
+    memset(v, 0, sizeof(*v));
+    v->cursor = c->view.cursor; v->population = c->view.population; v->rng = c->view.rng;
+    v->write_slot = c->write_slot; v->sample_slot = c->sample_slot; v->active = c->active; v->capacity = c->capacity;
+    v->transaction = c->transaction; v->fused = c->fused; v->layers = c->layers; v->reservoir_count = c->reservoir_count;
+    v->calls = c->calls; v->published = c->published; v->restores = c->restores; v->main_tokens = c->main_tokens;
+    v->arena_bytes = c->arena_bytes; v->gpu_bytes = c->gpu_bytes; v->host_bytes = c->host_bytes;
+    v->arena = c->arena; v->positions = c->positions; v->order = c->order; v->weights = c->weights;
+    v->cut0_sample_position = c->sample_slot >= 0 && c->cuts[0].positions ? c->cuts[0].positions[c->sample_slot] : -2;
+}
+
+void qwen_b200_ring_fail(Ring *c, int layer, int position) {
+    c->fail_layer = layer;
+    c->fail_position = position;
+}

@@ -136,6 +136,16 @@ const char *qwen_port_name(QwenPort);
  * fused path (no armed observer, owned K/V); returns -1 otherwise. */
 int qwen_generate(QwenSession *, int n, int *ids);
 
+/* B200 addition: the rest of the token opened by qwen_begin_token -- every layer
+ * and the readout -- as one CUDA graph replay when the session's runner serves
+ * every layer (owned K/V, or a cache backend that attached its arena to the
+ * runner, whose per-layer step callback is then not called) and no port is
+ * observed at this position; otherwise advance_layer until done, then
+ * finish_token. Must start at layer 0. Returns 0, -1, a layer's cache error, or
+ * -81 when a layer encoded a non-finite K/V row into its byte cache (the token
+ * is left open for abort, as after a failed layer). */
+int qwen_complete_token(QwenSession *);
+
 #ifdef __cplusplus
 }
 #endif

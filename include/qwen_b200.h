@@ -91,6 +91,54 @@ int qwen_b200_generate(QwenB200Runner *, int token, int position, int n, int *id
 int qwen_b200_enqueue(QwenB200Runner *, int token, int position, int n);
 int qwen_b200_last(QwenB200Runner *, TcmTop2 *top);
 
+/* ---- Bounded byte-codec K/V (the ring of include/bounded_cache.h) ----
+ * Layers whose cache slot is -1 keep their K/V in a ring arena in the
+ * reference layout (src/bounded_cache.h:26-28): per layer K codes
+ * [2][rows][128] int8, V codes [2][rows][128], scales [kind * 2 + head][rows]
+ * FP32, 528 bytes a row. The ring module owns the arena and the bookkeeping;
+ * the runner encodes the current rows and attends over the retained ones.
+ * Requires 2 KV heads. */
+typedef struct {
+    void *arena;         /* layers x rows x 528 bytes */
+    int rows;            /* physical rows: anchors + recent + reservoir */
+    int anchors, recent, reservoir;
+    void *save;          /* token cut row store: layers x 2 x 528 bytes */
+    float *logits_save;  /* token cut logits: vocab floats */
+    int positions;       /* logical capacity: the position limit of the runner */
+} QwenB200Ring;
+/* One token's ring bookkeeping, computed on the host. Retained rows are the
+ * first anchors_n anchor slots, the first reservoir_n reservoir slots and the
+ * first recent_n recent slots; reservoir rows add `bias` (the reference's
+ * weight * sqrt(128), src/qwen_cache.inc:34) to their scores when weighted. */
+typedef struct {
+    int write_slot, sample_slot;  /* sample_slot -1: no reservoir copy this token */
+    int anchors_n, reservoir_n, recent_n;
+    int weighted;
+    float bias;
+    int pad;
+} QwenB200RingStep;
+int qwen_b200_ring_attach(QwenB200Runner *, const QwenB200Ring *);
+/* The step the next qwen_b200_begin writes; begin then also takes the token cut
+ * (old write and sample rows of every layer and the logits into the save
+ * areas) and copies each layer's evicted row into the sample slot. */
+int qwen_b200_ring_stage(QwenB200Runner *, const QwenB200RingStep *);
+/* One layer's cache step: encode k, v (FP32 [2][128]) into the write slot and
+ * attend q over the retained rows into out. Device pointers. */
+int qwen_b200_ring_attention(QwenB200Runner *, int layer, const float *q, const float *k, const float *v, float *out);
+/* Synchronises; -1 when a row encoded since the last begin was non-finite. */
+int qwen_b200_ring_status(QwenB200Runner *);
+/* Every layer and the readout of the token opened by qwen_b200_begin, as one
+ * graph replay. 0; -3 non-finite logits; -4 a pipeline wait ran out; -5 a
+ * non-finite K/V row in a ring layer (the token must be aborted). */
+int qwen_b200_complete(QwenB200Runner *, TcmTop2 *top);
+/* 1 when qwen_b200_complete can run this runner's layers (every layer dense or
+ * served by an attached ring), else 0. */
+int qwen_b200_can_complete(const QwenB200Runner *);
+/* Token cut rows: mode 0 saves the write and sample rows of every layer into
+ * `save` and copies the old write row into the sample slot; mode 1 puts both
+ * saved rows back. Device pointers; sample_slot -1 skips the sample row. */
+void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int write_slot, int sample_slot, int mode);
+
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Measurement aid: mean device time (ms, CUDA events) of one standalone launch

@@ -5,9 +5,14 @@
  * checkpoints, the nested stack, token abort, reset, lineage, observer ports,
  * cache callbacks -- on the CPU, the way the reference's model-free lane does
  * (Makefile:58-83). No fused decoder exists there: models are built with
- * fused = 0 and every layer runs the primitive sequence. */
+ * fused = 0 and every layer runs the primitive sequence. The byte-codec cache
+ * entry points the CPU fake lacks are supplied as the reference's mechanics
+ * test supplies them (tests/bounded_mechanics.c:7-12), with the oracle's codec
+ * and ring attention (ring_cpu.h), plus a memcpy form of the token cut rows. */
 #include "../include/qwen_b200.h"
 #include "../include/tcm_seeded.h"
+#include "ring_cpu.h"
+#include <stdio.h>
 #include <string.h>
 
 void qwen_b200_seeded_fill(void *dst, int dtype, uint64_t seed, uint32_t id, size_t n, float offset, float scale) {
@@ -38,4 +43,55 @@ int qwen_b200_token(QwenB200Runner *r, int t, int p, TcmTop2 *o) { (void)r; (voi
 int qwen_b200_generate(QwenB200Runner *r, int t, int p, int n, int *i, TcmTop2 *o) {
     (void)r; (void)t; (void)p; (void)n; (void)i; (void)o;
     return -1;
+}
+
+int qwen_b200_complete(QwenB200Runner *r, TcmTop2 *t) { (void)r; (void)t; return -1; }
+int qwen_b200_can_complete(const QwenB200Runner *r) { (void)r; return 0; }
+int qwen_b200_ring_attach(QwenB200Runner *r, const QwenB200Ring *g) { (void)r; (void)g; return -1; }
+int qwen_b200_ring_stage(QwenB200Runner *r, const QwenB200RingStep *s) { (void)r; (void)s; return -1; }
+int qwen_b200_ring_attention(QwenB200Runner *r, int l, const float *q, const float *k, const float *v, float *o) {
+    (void)r; (void)l; (void)q; (void)k; (void)v; (void)o;
+    return -1;
+}
+int qwen_b200_ring_status(QwenB200Runner *r) { (void)r; return -1; }
+
+int gpu_encode_current(signed char *key, signed char *value, float *scales, const float *k, const float *v,
+                       int capacity, int position, int *invalid) {
+    *invalid = 0;
+    return orc_encode_rows(key, value, scales, k, v, capacity, position);
+}
+void gpu_ring_attention(TcmGpu *g, float *out, const float *q, const signed char *key, const signed char *value,
+                        const float *scales, float *scores, float *workspace, const int *order, const float *weights,
+                        int capacity, int length, int weighted) {
+    (void)g; (void)scores; (void)workspace;
+    orc_ring_attention_cpu(out, q, key, value, scales, order, weights, capacity, length, weighted);
+}
+/* The token cut rows (528 bytes: 4 code segments of 128, then 4 scales). */
+static void row_move(unsigned char *layer, int rows, int slot, unsigned char *buf, int to_buf) {
+    for (int seg = 0; seg < 4; seg++) {
+        unsigned char *a = layer + (size_t)(seg >> 1) * rows * 256 + ((size_t)(seg & 1) * rows + slot) * 128;
+        if (to_buf) memcpy(buf + seg * 128, a, 128);
+        else memcpy(a, buf + seg * 128, 128);
+    }
+    for (int j = 0; j < 4; j++) {
+        unsigned char *a = layer + (size_t)rows * 512 + ((size_t)j * rows + slot) * 4;
+        if (to_buf) memcpy(buf + 512 + j * 4, a, 4);
+        else memcpy(a, buf + 512 + j * 4, 4);
+    }
+}
+void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int write_slot, int sample_slot, int mode) {
+    for (int l = 0; l < layers; l++) {
+        unsigned char *layer = (unsigned char *)arena + (size_t)l * rows * 528;
+        unsigned char *s = (unsigned char *)save + (size_t)l * 2 * 528;
+        if (mode == 0) {
+            row_move(layer, rows, write_slot, s, 1);
+            if (sample_slot >= 0) {
+                row_move(layer, rows, sample_slot, s + 528, 1);
+                row_move(layer, rows, sample_slot, s, 0);
+            }
+        } else {
+            row_move(layer, rows, write_slot, s, 0);
+            if (sample_slot >= 0) row_move(layer, rows, sample_slot, s + 528, 0);
+        }
+    }
 }

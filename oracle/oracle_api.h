@@ -37,6 +37,21 @@ int orc_position(void *session);
 void orc_read_kv(void *session, int layer, int kind, float *out);
 /* The final-norm input x of the last pushed token (hidden floats). */
 void orc_read_hidden(void *session, float *out);
+/* Bounded byte-codec ring sessions (liboracle.so only). */
+typedef struct {
+    int cursor;
+    uint64_t population, rng;
+    int write_slot, sample_slot, active, rows;
+} OrcRingView;
+void *orc_ring_session_create(void *model, int logical, int anchors, int recent, int sample);
+/* View, slot positions [rows], order and weights [active], arena [layers][rows * 528]. */
+int orc_ring_read(void *session, OrcRingView *view, int *positions, int *order, float *weights, void *arena);
+/* The reference CPU codec for one row of 128 (src/byte_codec.h:5-9). */
+int orc_codec(const float *x, int8_t *codes, float *scale);
+/* Ring attention over int8 rows (src/qwen_cache.inc:31-43), 12 query / 2 KV heads of 128. */
+void orc_ring_attention(float *out, const float *q, const signed char *key, const signed char *value,
+                        const float *scales, const int *order, const float *weights, int capacity, int length,
+                        int weighted);
 /* Seeded weight element readback for generator pinning: tensor id, index. */
 float orc_weight_value(void *model, uint32_t tensor, uint64_t index);
 #ifdef __cplusplus

@@ -20,6 +20,7 @@
  */
 #include "oracle_api.h"
 #include "par.h"
+#include "ring_cpu.h"
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -32,10 +33,23 @@ typedef struct {
     float *embedding, *norm;
     OrcLayer *layer;
 } OrcModel;
+/* Bounded anchors/recent/reservoir byte-codec cache (src/bounded_cache.h):
+ * physical rows, the slot of each retained position (-1 empty), the view
+ * (cursor, evictions, SplitMix64 state) and the arena in the reference layout,
+ * per layer [K codes 2 x rows x 128][V codes][scales 4 x rows]. */
+typedef struct {
+    int anchors, recent, sample, rows, write_slot, sample_slot, active;
+    int cursor;
+    uint64_t population, rng;
+    int *positions, *order;
+    float *weights;
+    unsigned char *arena;
+} OrcRing;
 typedef struct {
     const OrcModel *model;
     int position, capacity;
     float *keys, *values, *x, *norm, *q, *k, *v, *attention, *projected, *gate, *up, *logits, *scores;
+    OrcRing *ring;
 } OrcSession;
 
 typedef struct { float *p; uint64_t base; TcmFill f; int bf16; } FillJob;
@@ -58,7 +72,7 @@ void *orc_model_create(const OrcShape *shape, uint64_t seed, const TcmFillLaw *l
     OrcModel *m = calloc(1, sizeof(*m));
     if (!m) abort();
     m->shape = *shape;
-    int d = shape->hidden, kv = shape->kvheads * shape->head, f = shape->intermediate;
+    int d = shape->hidden, qd = shape->qheads * shape->head, kv = shape->kvheads * shape->head, f = shape->intermediate;
     /* Matrices follow the requested storage; vectors stay FP32 (profile 2 keeps
      * vectors FP32, src/qwen_weights.inc:13). */
     m->embedding = tensor(seed, law, 0, (size_t)shape->vocab * d, bf16);
@@ -69,13 +83,13 @@ void *orc_model_create(const OrcShape *shape, uint64_t seed, const TcmFillLaw *l
         OrcLayer *L = &m->layer[l];
         L->input_norm = tensor(seed, law, tcm_layer_tensor(l, TCM_T_INPUT_NORM), (size_t)d, 0);
         L->post_norm = tensor(seed, law, tcm_layer_tensor(l, TCM_T_POST_NORM), (size_t)d, 0);
-        L->q = tensor(seed, law, tcm_layer_tensor(l, TCM_T_Q), (size_t)d * d, bf16);
+        L->q = tensor(seed, law, tcm_layer_tensor(l, TCM_T_Q), (size_t)qd * d, bf16);
         L->k = tensor(seed, law, tcm_layer_tensor(l, TCM_T_K), (size_t)kv * d, bf16);
         L->v = tensor(seed, law, tcm_layer_tensor(l, TCM_T_V), (size_t)kv * d, bf16);
-        L->qb = tensor(seed, law, tcm_layer_tensor(l, TCM_T_QB), (size_t)d, 0);
+        L->qb = tensor(seed, law, tcm_layer_tensor(l, TCM_T_QB), (size_t)qd, 0);
         L->kb = tensor(seed, law, tcm_layer_tensor(l, TCM_T_KB), (size_t)kv, 0);
         L->vb = tensor(seed, law, tcm_layer_tensor(l, TCM_T_VB), (size_t)kv, 0);
-        L->o = tensor(seed, law, tcm_layer_tensor(l, TCM_T_O), (size_t)d * d, bf16);
+        L->o = tensor(seed, law, tcm_layer_tensor(l, TCM_T_O), (size_t)d * qd, bf16);
         L->gate = tensor(seed, law, tcm_layer_tensor(l, TCM_T_GATE), (size_t)f * d, bf16);
         L->up = tensor(seed, law, tcm_layer_tensor(l, TCM_T_UP), (size_t)f * d, bf16);
         L->down = tensor(seed, law, tcm_layer_tensor(l, TCM_T_DOWN), (size_t)d * f, bf16);
@@ -117,8 +131,8 @@ void *orc_session_create(void *p, int capacity) {
     size_t kv = (size_t)S->layers * S->kvheads * capacity * S->head;
 #define ORC_ALLOC(field, n) do { s->field = calloc((size_t)(n), sizeof(float)); if (!s->field) abort(); } while (0)
     ORC_ALLOC(keys, kv); ORC_ALLOC(values, kv); ORC_ALLOC(x, S->hidden); ORC_ALLOC(norm, S->hidden);
-    ORC_ALLOC(q, S->hidden); ORC_ALLOC(k, S->kvheads * S->head); ORC_ALLOC(v, S->kvheads * S->head);
-    ORC_ALLOC(attention, S->hidden); ORC_ALLOC(projected, S->hidden); ORC_ALLOC(gate, S->intermediate);
+    ORC_ALLOC(q, S->qheads * S->head); ORC_ALLOC(k, S->kvheads * S->head); ORC_ALLOC(v, S->kvheads * S->head);
+    ORC_ALLOC(attention, S->qheads * S->head); ORC_ALLOC(projected, S->hidden); ORC_ALLOC(gate, S->intermediate);
     ORC_ALLOC(up, S->intermediate); ORC_ALLOC(logits, S->vocab); ORC_ALLOC(scores, (size_t)S->qheads * capacity);
 #undef ORC_ALLOC
     return s;
@@ -129,6 +143,13 @@ void orc_session_free(void *p) {
     if (!s) return;
     float *all[] = {s->keys, s->values, s->x, s->norm, s->q, s->k, s->v, s->attention, s->projected, s->gate, s->up, s->logits, s->scores};
     for (unsigned i = 0; i < sizeof(all) / sizeof(all[0]); i++) free(all[i]);
+    if (s->ring) {
+        free(s->ring->positions);
+        free(s->ring->order);
+        free(s->ring->weights);
+        free(s->ring->arena);
+        free(s->ring);
+    }
     free(s);
 }
 
@@ -213,27 +234,165 @@ static OrcTop2 top2(const float *p, int n) {
     return r;
 }
 
+/* ------------------------------------------------------------------ bounded ring
+ * The reference's retention policy, src/bounded_cache.h:
+ *   ring_random / ring_draw  :24-25  SplitMix64 (state starts at 7) and an
+ *                                     unbiased draw in [0, n) by rejection below
+ *                                     (2^64 - n) mod n;
+ *   ring_order               :51-57  retained slots sorted by position; reservoir
+ *                                     slots weigh log(population / min(population,
+ *                                     reservoir)), the others 0;
+ *   ring_begin               :71-74  the write slot (anchors first, then the
+ *                                     recent ring); overwriting a retained row is
+ *                                     an eviction, offered to the reservoir
+ *                                     (filled in order, then replaced with
+ *                                     probability reservoir / evictions);
+ *   ring_step / ring_copy_row :38-46,65  per layer: the sampled row copied from
+ *                                     the evicted slot, the current K/V encoded
+ *                                     into the write slot, ring attention. */
+static uint64_t ring_next(OrcRing *r) {
+    uint64_t z = (r->rng += UINT64_C(0x9e3779b97f4a7c15));
+    z = (z ^ (z >> 30)) * UINT64_C(0xbf58476d1ce4e5b9);
+    z = (z ^ (z >> 27)) * UINT64_C(0x94d049bb133111eb);
+    return z ^ (z >> 31);
+}
+static uint64_t ring_draw(OrcRing *r, uint64_t n) {
+    uint64_t x, t = (uint64_t)(-n) % n;
+    do x = ring_next(r); while (x < t);
+    return x % n;
+}
+static const int *sort_positions;
+static int by_position(const void *a, const void *b) {
+    int pa = sort_positions[*(const int *)a], pb = sort_positions[*(const int *)b];
+    return (pa > pb) - (pa < pb);
+}
+static void ring_order(OrcRing *r) {
+    r->active = 0;
+    for (int i = 0; i < r->rows; i++)
+        if (r->positions[i] >= 0) r->order[r->active++] = i;
+    sort_positions = r->positions; /* positions are distinct: the order is unique */
+    qsort(r->order, (size_t)r->active, sizeof(int), by_position);
+    int m = r->population < (uint64_t)r->sample ? (int)r->population : r->sample;
+    for (int i = 0; i < r->active; i++)
+        r->weights[i] = (r->order[i] >= r->anchors + r->recent && m) ? logf((float)r->population / (float)m) : 0;
+}
+static void ring_begin(OrcRing *r, int p) {
+    r->sample_slot = -1;
+    r->write_slot = p < r->anchors ? p : r->anchors + (p - r->anchors) % r->recent;
+    if (r->positions[r->write_slot] >= 0) {
+        r->population++;
+        if (r->sample) {
+            uint64_t n = r->population, j = n <= (uint64_t)r->sample ? n - 1 : ring_draw(r, n);
+            if (j < (uint64_t)r->sample) {
+                r->sample_slot = r->anchors + r->recent + (int)j;
+                r->positions[r->sample_slot] = r->positions[r->write_slot];
+            }
+        }
+    }
+    r->positions[r->write_slot] = p;
+    r->cursor = p + 1;
+    ring_order(r);
+}
+static unsigned char *ring_layer(OrcRing *r, int l) { return r->arena + (size_t)l * r->rows * ORC_RING_ROW_BYTES; }
+/* ring_copy_row: the evicted row (still intact in this layer) into the sample slot. */
+static void ring_copy_row(OrcRing *r, int l, int to, int from) {
+    unsigned char *base = ring_layer(r, l);
+    float *scales = (float *)(base + (size_t)r->rows * 512);
+    for (int kind = 0; kind < 2; kind++)
+        for (int h = 0; h < ORC_RING_KV; h++) {
+            unsigned char *codes = base + (size_t)kind * r->rows * 256;
+            memcpy(codes + ((size_t)h * r->rows + to) * 128, codes + ((size_t)h * r->rows + from) * 128, 128);
+            scales[(kind * 2 + h) * r->rows + to] = scales[(kind * 2 + h) * r->rows + from];
+        }
+}
+static int ring_layer_step(OrcSession *s, int l) {
+    OrcRing *r = s->ring;
+    unsigned char *base = ring_layer(r, l);
+    if (r->sample_slot >= 0) ring_copy_row(r, l, r->sample_slot, r->write_slot);
+    if (orc_encode_rows((signed char *)base, (signed char *)base + (size_t)r->rows * 256,
+                        (float *)(base + (size_t)r->rows * 512), s->k, s->v, r->rows, r->write_slot))
+        return -81;
+    orc_ring_attention_cpu(s->attention, s->q, (const signed char *)base, (const signed char *)base + (size_t)r->rows * 256,
+                           (const float *)(base + (size_t)r->rows * 512), r->order, r->weights, r->rows, r->active,
+                           r->sample && r->population > 0);
+    return 0;
+}
+
+void *orc_ring_session_create(void *model, int logical, int anchors, int recent, int sample) {
+    const OrcModel *m = model;
+    const OrcShape *S = &m->shape;
+    if (recent < 1 || anchors < 0 || sample < 0 || anchors + recent + sample > logical || logical > S->max_position ||
+        S->kvheads != ORC_RING_KV || S->head != ORC_RING_HEAD || S->qheads != ORC_RING_KV * ORC_RING_GROUP)
+        return NULL;
+    OrcSession *s = orc_session_create(model, 1);
+    free(s->keys);
+    free(s->values);
+    s->keys = s->values = NULL;
+    s->capacity = logical;
+    OrcRing *r = calloc(1, sizeof(*r));
+    if (!r) abort();
+    r->anchors = anchors; r->recent = recent; r->sample = sample; r->rows = anchors + recent + sample;
+    r->rng = 7;
+    r->positions = malloc((size_t)r->rows * sizeof(int));
+    r->order = malloc((size_t)r->rows * sizeof(int));
+    r->weights = malloc((size_t)r->rows * sizeof(float));
+    r->arena = calloc((size_t)S->layers * r->rows, ORC_RING_ROW_BYTES);
+    if (!r->positions || !r->order || !r->weights || !r->arena) abort();
+    for (int i = 0; i < r->rows; i++) r->positions[i] = -1;
+    s->ring = r;
+    return s;
+}
+
+int orc_ring_read(void *session, OrcRingView *view, int *positions, int *order, float *weights, void *arena) {
+    OrcSession *s = session;
+    OrcRing *r = s->ring;
+    if (!r) return -1;
+    if (view) {
+        view->cursor = r->cursor; view->population = r->population; view->rng = r->rng;
+        view->write_slot = r->write_slot; view->sample_slot = r->sample_slot; view->active = r->active;
+        view->rows = r->rows;
+    }
+    if (positions) memcpy(positions, r->positions, (size_t)r->rows * sizeof(int));
+    if (order) memcpy(order, r->order, (size_t)r->active * sizeof(int));
+    if (weights) memcpy(weights, r->weights, (size_t)r->active * sizeof(float));
+    if (arena) memcpy(arena, r->arena, (size_t)s->model->shape.layers * r->rows * ORC_RING_ROW_BYTES);
+    return 0;
+}
+
+int orc_codec(const float *x, int8_t *codes, float *scale) { return orc_codec_row(x, codes, scale); }
+
+void orc_ring_attention(float *out, const float *q, const signed char *key, const signed char *value,
+                        const float *scales, const int *order, const float *weights, int capacity, int length,
+                        int weighted) {
+    orc_ring_attention_cpu(out, q, key, value, scales, order, weights, capacity, length, weighted);
+}
+
 int orc_push(void *p, int token, OrcTop2 *top, float *logits) {
     OrcSession *s = p;
     const OrcModel *m = s->model;
     const OrcShape *S = &m->shape;
     if (token < 0 || token >= S->vocab || s->position >= s->capacity) return -1;
-    int d = S->hidden, kv = S->kvheads * S->head, f = S->intermediate;
+    int d = S->hidden, qd = S->qheads * S->head, kv = S->kvheads * S->head, f = S->intermediate;
+    if (s->ring) ring_begin(s->ring, s->position);
     memcpy(s->x, m->embedding + (size_t)token * d, (size_t)d * 4);
     for (int l = 0; l < S->layers; l++) {
         const OrcLayer *L = &m->layer[l];
         rms(s->norm, s->x, L->input_norm, d, S->epsilon);
-        matvec(L->q, d, d, s->norm, s->q); add(s->q, L->qb, d);
+        matvec(L->q, d, qd, s->norm, s->q); add(s->q, L->qb, qd);
         matvec(L->k, d, kv, s->norm, s->k); add(s->k, L->kb, kv);
         matvec(L->v, d, kv, s->norm, s->v); add(s->v, L->vb, kv);
         rope(s->q, S->qheads, S->head, s->position, S->theta);
         rope(s->k, S->kvheads, S->head, s->position, S->theta);
-        size_t base = (size_t)l * S->kvheads * s->capacity * S->head;
-        cache_append(s->keys + base, s->k, S->kvheads, S->head, s->capacity, s->position);
-        cache_append(s->values + base, s->v, S->kvheads, S->head, s->capacity, s->position);
-        attention(s->attention, s->q, s->keys + base, s->values + base, s->scores, S->qheads, S->kvheads, S->head,
-                  s->capacity, s->position + 1);
-        matvec(L->o, d, d, s->attention, s->projected);
+        if (s->ring) {
+            if (ring_layer_step(s, l)) return -81;
+        } else {
+            size_t base = (size_t)l * S->kvheads * s->capacity * S->head;
+            cache_append(s->keys + base, s->k, S->kvheads, S->head, s->capacity, s->position);
+            cache_append(s->values + base, s->v, S->kvheads, S->head, s->capacity, s->position);
+            attention(s->attention, s->q, s->keys + base, s->values + base, s->scores, S->qheads, S->kvheads, S->head,
+                      s->capacity, s->position + 1);
+        }
+        matvec(L->o, qd, d, s->attention, s->projected);
         add(s->x, s->projected, d);
         rms(s->norm, s->x, L->post_norm, d, S->epsilon);
         matvec(L->gate, d, f, s->norm, s->gate);

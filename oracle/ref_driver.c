@@ -60,7 +60,7 @@ void *orc_model_create(const OrcShape *S, uint64_t seed, const TcmFillLaw *law, 
     m->eos = -1; m->eos_extra = 0;
     memset(m->digest, 'a', 64);
     memset(m->identity, 'b', 64);
-    int d = S->hidden, kv = S->kvheads * S->head, f = S->intermediate;
+    int d = S->hidden, qd = S->qheads * S->head, kv = S->kvheads * S->head, f = S->intermediate;
     m->embedding = upload(r, seed, law, 0, 2, S->vocab, d, bf16);
     m->norm = upload(r, seed, law, 1, 1, d, 0, 0);
     m->layer = calloc((size_t)S->layers, sizeof(QwenLayer));
@@ -69,13 +69,13 @@ void *orc_model_create(const OrcShape *S, uint64_t seed, const TcmFillLaw *law, 
         QwenLayer *L = &m->layer[l];
         L->input_norm = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_INPUT_NORM), 1, d, 0, 0);
         L->post_norm = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_POST_NORM), 1, d, 0, 0);
-        L->q = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_Q), 2, d, d, bf16);
+        L->q = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_Q), 2, qd, d, bf16);
         L->k = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_K), 2, kv, d, bf16);
         L->v = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_V), 2, kv, d, bf16);
-        L->qb = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_QB), 1, d, 0, 0);
+        L->qb = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_QB), 1, qd, 0, 0);
         L->kb = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_KB), 1, kv, 0, 0);
         L->vb = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_VB), 1, kv, 0, 0);
-        L->o = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_O), 2, d, d, bf16);
+        L->o = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_O), 2, d, qd, bf16);
         L->gate = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_GATE), 2, f, d, bf16);
         L->up = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_UP), 2, f, d, bf16);
         L->down = upload(r, seed, law, tcm_layer_tensor(l, TCM_T_DOWN), 2, d, f, bf16);

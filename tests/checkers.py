@@ -77,3 +77,48 @@ class CpuDecoder:
     def close(self):
         self.L.orc_session_free(self.session)
         self.L.orc_model_free(self.model)
+
+
+class OrcRingView(ctypes.Structure):
+    _fields_ = [("cursor", c_int), ("population", c_uint64), ("rng", c_uint64)] + [
+        (n, c_int) for n in ("write_slot", "sample_slot", "active", "rows")]
+
+
+class OracleRing(CpuDecoder):
+    """The oracle's bounded byte-codec session (liboracle.so only)."""
+
+    def __init__(self, shape: Shape, seed: int, law: FillLaw, bf16: bool, logical: int, anchors: int, recent: int,
+                 sample: int):
+        self.L = load(ORACLE)
+        self.L.orc_ring_session_create.restype = c_void_p
+        self.L.orc_ring_session_create.argtypes = [c_void_p, c_int, c_int, c_int, c_int]
+        self.L.orc_ring_read.argtypes = [c_void_p, POINTER(OrcRingView), c_void_p, c_void_p, c_void_p, c_void_p]
+        self.shape = shape
+        self.model = self.L.orc_model_create(ctypes.byref(shape), seed, ctypes.byref(law), int(bf16))
+        self.session = self.L.orc_ring_session_create(self.model, logical, anchors, recent, sample)
+        assert self.session, "oracle refused the ring"
+        self.rows = anchors + recent + sample
+
+    def state(self):
+        v = OrcRingView()
+        pos = np.empty(self.rows, np.int32)
+        order = np.empty(self.rows, np.int32)
+        weights = np.empty(self.rows, np.float32)
+        arena = np.empty(self.shape.layers * self.rows * 528, np.uint8)
+        self.L.orc_ring_read(self.session, ctypes.byref(v), c_void_p(pos.ctypes.data), c_void_p(order.ctypes.data),
+                             c_void_p(weights.ctypes.data), c_void_p(arena.ctypes.data))
+        return dict(view=(v.cursor, v.population, v.rng), slots=(v.write_slot, v.sample_slot), active=v.active,
+                    positions=pos, order=order[:v.active], weights=weights[:v.active], arena=arena)
+
+
+def codec_rows(x: np.ndarray):
+    """The oracle's byte codec (src/byte_codec.h:5-9) over rows of 128: codes, scales."""
+    L = load(ORACLE)
+    L.orc_codec.argtypes = [c_void_p, c_void_p, c_void_p]
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, 128)
+    codes = np.empty(x.shape, np.int8)
+    scales = np.empty(x.shape[0], np.float32)
+    for i in range(x.shape[0]):
+        assert L.orc_codec(c_void_p(x[i].ctypes.data), c_void_p(codes[i].ctypes.data),
+                           c_void_p(scales[i:].ctypes.data)) == 0
+    return codes, scales

@@ -202,3 +202,80 @@ def test_top2_random_and_ties():
             assert top.second == order[1]
         L.gpu_free(d)
     L.gpu_close(g)
+
+
+def test_byte_codec_and_ring_attention_primitives():
+    """gpu_encode_current bit for bit against the reference codec
+    (src/byte_codec.h:5-9, via the oracle) including a zero row and a refused
+    non-finite row; gpu_byte_attention and gpu_ring_attention (gathered rows,
+    reservoir weights) within the attention tolerance of the oracle's CPU
+    restatement of src/qwen_cache.inc:20-43."""
+    import ctypes
+    from checkers import ORACLE, codec_rows, load
+    L = cm.lib()
+    O = load(ORACLE)
+    O.orc_ring_attention.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int] * 3
+    rng = np.random.default_rng(9)
+    capacity, length = 300, 260
+    key, value = L.gpu_alloc(2 * capacity * 128), L.gpu_alloc(2 * capacity * 128)
+    scales, invalid = L.gpu_alloc(4 * capacity * 4), L.gpu_alloc(4)
+    L.gpu_zero(key, 2 * capacity * 128)
+    L.gpu_zero(value, 2 * capacity * 128)
+    L.gpu_zero(scales, 4 * capacity * 4)
+    want_codes = np.zeros((2, 2, capacity, 128), np.int8)
+    want_scales = np.zeros((4, capacity), np.float32)
+    for p in range(length):
+        k = (rng.standard_normal(256) * (0.1 + p % 7)).astype(np.float32)
+        v = (rng.standard_normal(256) * (0.5 + p % 3)).astype(np.float32)
+        if p == 3:
+            k[:] = 0
+        dk, dv = dev(k), dev(v)
+        assert L.gpu_encode_current(key, value, scales, dk, dv, capacity, p, invalid) == 0
+        for kind, x in enumerate((k, v)):
+            c, s = codec_rows(x.reshape(2, 128))
+            want_codes[kind, :, p] = c
+            want_scales[kind * 2:kind * 2 + 2, p] = s
+        L.gpu_free(dk)
+        L.gpu_free(dv)
+    bad = np.ones(256, np.float32)
+    bad[17] = np.nan
+    db = dev(bad)
+    assert L.gpu_encode_current(key, value, scales, db, db, capacity, length, invalid) == -1
+    L.gpu_free(db)
+    got_k = host(key, 2 * capacity * 128, np.int8).reshape(2, capacity, 128)
+    got_v = host(value, 2 * capacity * 128, np.int8).reshape(2, capacity, 128)
+    got_s = host(scales, 4 * capacity).reshape(4, capacity)
+    assert np.array_equal(got_k[:, :length], want_codes[0, :, :length])
+    assert np.array_equal(got_v[:, :length], want_codes[1, :, :length])
+    assert np.array_equal(got_s[:, :length].view(np.uint32), want_scales[:, :length].view(np.uint32))
+    assert want_scales[0, 3] == 1.0  # a zero row keeps scale 1
+
+    q = rng.standard_normal(12 * 128).astype(np.float32)
+    dq, out = dev(q), L.gpu_alloc(12 * 128 * 4)
+    kh = np.ascontiguousarray(got_k)
+    vh = np.ascontiguousarray(got_v)
+    sh = np.ascontiguousarray(got_s)
+    g = L.gpu_open()
+    cases = [("byte", np.arange(length, dtype=np.int32), np.zeros(length, np.float32), 0),
+             ("ring", rng.permutation(length)[:200].astype(np.int32), np.zeros(200, np.float32), 0),
+             ("ring-weighted", rng.permutation(length)[:217].astype(np.int32),
+              np.where(np.arange(217) % 3 == 0, 0.7, 0.0).astype(np.float32), 1)]
+    for name, order, weights, weighted in cases:
+        n = len(order)
+        if name == "byte":
+            L.gpu_byte_attention(g, out, dq, key, value, scales, None, None, capacity, n)
+        else:
+            do, dw = dev(order), dev(weights)
+            L.gpu_ring_attention(g, out, dq, key, value, scales, None, None, do, dw, capacity, n, weighted)
+            L.gpu_sync()
+            L.gpu_free(do)
+            L.gpu_free(dw)
+        want = np.empty(12 * 128, np.float32)
+        O.orc_ring_attention(ptr(want), ptr(q), ptr(kh), ptr(vh), ptr(sh), ptr(order), ptr(weights), capacity, n,
+                             weighted)
+        err = float(np.max(np.abs(host(out, 12 * 128) - want)))
+        print(f"{name}: {n} rows, max |gpu - oracle| = {err:.2e}")
+        assert err < 2e-5, name
+    for p in (key, value, scales, invalid, dq, out):
+        L.gpu_free(p)
+    L.gpu_close(g)

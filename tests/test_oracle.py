@@ -113,3 +113,33 @@ def test_seeded_generator_statistics():
     assert abs(vals.mean()) < 0.002
     assert abs(vals.std() - 0.02) < 0.001
     assert np.max(np.abs(vals)) <= 6 * 0.02
+
+
+REF_RING = REF_CPU.parent / "libref_ring.so"
+
+
+@pytest.mark.skipif(not REF_RING.exists(), reason="reference sources not built here")
+def test_oracle_ring_bit_exact_with_reference_ring():
+    """The oracle's bounded byte-codec session against the reference's
+    src/bounded_cache.h over the reference host (oracle/_ref/libref_ring.so):
+    arena bytes, slot positions, cursor / evictions / RNG, order, weights and
+    logits bit for bit over 40 tokens at (2, 4, 3), which evicts from token 7 on."""
+    import ctypes as C
+    from checkers import OracleRing
+    from test_ring_cpu import SEED, SHAPE, RefRing
+    ours = OracleRing(SHAPE, SEED, cm.TEST_LAW, False, 1024, 2, 4, 3)
+    ref = RefRing(1024, 2, 4, 3)
+    try:
+        for i in range(40):
+            token = (i * 7 + 3) % SHAPE.vocab
+            top, logits = ours.push(token)
+            assert ref.push(token) == 0
+            a, b = ours.state(), ref.snapshot()
+            assert a["view"] == b["view"] and a["slots"] == b["slots"] and a["active"] == b["active"]
+            assert np.array_equal(a["positions"], b["positions"]) and np.array_equal(a["order"], b["order"])
+            assert np.array_equal(a["weights"].view(np.uint32), b["weights"])
+            assert np.array_equal(a["arena"], b["arena"]), f"token {i}"
+            assert np.array_equal(logits.view(np.uint32), b["logits"]), f"token {i}"
+        assert a["view"][1] == 34 and a["active"] == 9
+    finally:
+        ours.close()
