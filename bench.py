@@ -13,8 +13,13 @@ positions 512..767 (each 256-step segment restarts from the post-prompt state).
           pinned host->device copy of the token state, one graph replay and one
           device->host read of the top-2, host synchronised every step.
 
+With --config bf16-bounded a step is one token of each of the GPU's bounded
+sessions through ring_push (include/bounded_cache.h), which reads the top-2 back
+every token by design (abort and recovery are decided per token on the host):
+value is CUDA-event time over those steps, e2e the host clock over a second pass.
+
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-       [--config fp32-ctx512 | bf16-ctx4096 | fp32-2layer]
+       [--config fp32-ctx512 | bf16-ctx4096 | fp32-2layer | bf16-bounded]
 Under torchrun (N > 1) every rank runs its own replica; rank 0 prints one JSON line.
 """
 from __future__ import annotations
@@ -41,6 +46,14 @@ CONFIGS = {
     "bf16-ctx4096": dict(layers=28, profile=2, prompt=4096, window=512),
     # The reduced 2-layer model of the reference's CPU-runnable case (64 + 32).
     "fp32-2layer": dict(layers=2, profile=0, prompt=64, window=32),
+    # Bounded compressed memory: full Qwen2.5-1.5B, source-BF16 weights, all-layer
+    # K/V in the byte codec with 64 anchor, 1024 recent and 1024 reservoir rows,
+    # logical context 32768; two sessions per GPU (16 over 8 GPUs), each prefilled
+    # past the first 1,024 evictions, then streaming with a mark every 256 tokens
+    # (nested to depth 2, the reference ring's limit), a commit 128 tokens later,
+    # and one injected layer failure with recovery per 1,024 tokens.
+    "bf16-bounded": dict(layers=28, profile=2, ring=(64, 1024, 1024), logical=32768, prefill=2200,
+                         sessions=2, mark_every=256, fail_every=1024),
 }
 
 
@@ -190,6 +203,159 @@ def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: 
     return total / wall, n, sample, kind, first_logits
 
 
+def cpu_reference_ring_rate(cfg, threads: int | None = None):
+    """The reference's own bounded cache (src/bounded_cache.h over src/qwen.c and
+    tests/gpu_stub.c, oracle/_ref/libref_ring.so) on the host cores, one ring
+    session per thread with the benchmark's retention, each pushing a 2-token
+    prompt and greedy steps from position 0 (the retained set is still small
+    there; at 2,112 retained rows ring attention adds about 1% to a token's
+    arithmetic). Returns (tokens/s, threads, sample, kind) or None."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import ctypes
+    ref = ROOT / "oracle" / "_ref" / "libref_ring.so"
+    if not ref.exists():
+        return None
+    import cmachine_b200 as cm
+    from checkers import load
+    L = load(ref)
+    L.rr_open.restype = ctypes.c_void_p
+    L.rr_open.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.rr_push.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    L.rr_close.argtypes = [ctypes.c_void_p]
+    shape = cm.qwen_shape(cfg["layers"], 4096)
+    model = L.orc_model_create(ctypes.byref(shape), 2026, ctypes.byref(cm.BENCH_LAW), int(cfg["profile"] == 2))
+    n = threads or max(1, min(os.cpu_count() or 1, 16))
+    steps, results = 6, [0] * n
+    a, r, m = cfg["ring"]
+
+    def worker(i):
+        h = L.rr_open(model, 4096, a, r, m, 0)
+        for t in prompt_tokens(90 + i, 2 + steps, shape.vocab):
+            assert L.rr_push(h, t) == 0
+            results[i] += 1
+        L.rr_close(h)
+
+    t0 = time.perf_counter()
+    pool = [threading.Thread(target=worker, args=(i,)) for i in range(n)]
+    for th in pool:
+        th.start()
+    for th in pool:
+        th.join()
+    wall = time.perf_counter() - t0
+    L.orc_model_free(model)
+    sample = (f"{n} threads x 8 ring_push tokens from position 0, 28-layer BF16 seeded model, retention "
+              f"({a}, {r}, {m}), one bounded session per thread")
+    return sum(results) / wall, n, sample, "reference"
+
+
+def run_bounded(args, cfg, world, rank, local, dist, torch):
+    """Bounded byte-codec sessions (ring_push), two per GPU."""
+    import cmachine_b200 as cm
+    L = cm.lib()
+    L.qwen_b200_set_device(local)
+    shape = cm.qwen_shape(cfg["layers"], cfg["logical"])
+    model = cm.Model(shape, 2026 + rank, cm.BENCH_LAW, cfg["profile"])
+    a, r, m = cfg["ring"]
+    rings = [cm.Ring(model, cfg["logical"], a, r, m) for _ in range(cfg["sessions"])]
+    assert all(g.view().fused for g in rings)
+    for i, g in enumerate(rings):
+        for t in prompt_tokens(7 + 16 * rank + i, cfg["prefill"], shape.vocab):
+            assert g.push(t) == 0
+    state = [dict(count=0, frames=[]) for _ in rings]
+    counts = {"tokens": 0, "marks": 0, "commits": 0, "failures": 0}
+
+    def step():
+        for g, st in zip(rings, state):
+            sv = g.session.view()
+            if st["count"] % cfg["fail_every"] == cfg["fail_every"] // 2:
+                g.fail(27, sv.position)  # injected failure, then recovery by a retry
+                assert g.push(sv.pending) == -77
+                counts["failures"] += 1
+            assert g.push(sv.pending) == 0
+            counts["tokens"] += 1
+            st["count"] += 1
+            if st["count"] % cfg["mark_every"] == 0 and len(st["frames"]) < 2:
+                status, frame = g.mark()
+                assert status == 0
+                st["frames"].append(frame)
+                counts["marks"] += 1
+            elif st["count"] % cfg["mark_every"] == cfg["mark_every"] // 2 and st["frames"]:
+                assert g.commit(st["frames"].pop()) == 0
+                counts["commits"] += 1
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    L.gpu_sync()
+    for key in counts:
+        counts[key] = 0
+    barrier(dist, torch)
+    with ClockSampler(local) as clocks:
+        L.qwen_b200_mark(0)
+        for _ in range(args.steps):
+            step()
+        L.qwen_b200_mark(1)
+        L.gpu_sync()
+        device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    timed = dict(counts)
+    barrier(dist, torch)
+    device_ms = max_over_ranks(device_ms, dist, torch)
+    # End to end: a second pass on the host clock.
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, dist, torch)
+    barrier(dist, torch)
+
+    runner = rings[0].session.runner
+    pos = rings[0].session.view().position
+    es = 2
+    gateup_ms = L.qwen_b200_time_stage(runner, 3, 0, pos - 1, 30)
+    gateup_bytes = 2 * shape.intermediate * shape.hidden * es + shape.intermediate * 4
+    ring_ms = L.qwen_b200_time_stage(runner, 1, 0, pos - 1, 30)
+    peak, peak_kind = measured_peaks()
+    achieved = gateup_bytes / (gateup_ms * 1e-3) / 1e9
+    active = rings[0].view().active
+    ring_bytes = shape.layers * active * 528 + 2 * shape.layers * 2 * 528 + 2 * shape.vocab * 4
+    step_bytes = model.weight_bytes + ring_bytes
+    tokens = timed["tokens"] * world
+    ms_per_token = device_ms / max(timed["tokens"], 1)
+    views = [g.view() for g in rings]
+    for g in rings:
+        g.close()
+    model.free()
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("gateup_bf16")
+    return {
+        "metric": METRIC, "value": round(tokens / (device_ms * 1e-3), 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(device_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16-weights/f32/int8-kv", "data": "synthetic",
+        "config": {"workload": "qwen2.5-1.5b-bf16-bounded", "layers": shape.layers, "batch": 1,
+                   "sessions_per_gpu": cfg["sessions"], "sessions_total": cfg["sessions"] * world,
+                   "retention": {"anchors": a, "recent": r, "reservoir": m}, "logical_context": cfg["logical"],
+                   "prefill_tokens": cfg["prefill"], "retained_rows": active,
+                   "timed_ops_per_rank": timed, "parallelism": f"replicas{world}",
+                   "weights": "seeded N(0,0.02) random init",
+                   "l2": "inputs larger than L2 (weights stream from HBM every token)"},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 64 * len(rings),
+                "d2h_bytes_per_step": 64 * len(rings)},
+        "gpu_launches": (5 * shape.layers + 2) * (timed["tokens"] + timed["failures"]),
+        "roofline": {"bound": "hbm", "kernel": "gateup_kernel (RMSNorm + gate/up GEMV + SwiGLU)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": gateup_bytes,
+                     "launch_ms": round(gateup_ms, 5)},
+        "step_roofline": {"bytes_per_token": int(step_bytes),
+                          "achieved_gbs": round(step_bytes / (ms_per_token * 1e6), 1),
+                          "frac": round(step_bytes / (ms_per_token * 1e6) / peak, 4)},
+        "ring_attention_ms_layer0": round(ring_ms, 5),
+        "ring_state": [{"position": v.cursor, "evictions": v.population, "retained": v.active,
+                        "restores": v.restores} for v in views],
+        "clocks": clocks.summary(),
+    }
+
+
 def gpu_dlogit(layers: int, profile: int, ref_logits):
     """max |delta logit| of the GPU path on the CPU sample's first thread."""
     import numpy as np
@@ -327,7 +493,14 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
-        rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
+        if "ring" in cfg:
+            got = cpu_reference_ring_rate(cfg)
+            if got is None:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference ring build (oracle/_ref) is absent"}))
+                return
+            rate, cores, sample, kind = got
+        else:
+            rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
         print(json.dumps({
             "metric": METRIC, "impl": "reference", "value": round(rate, 4), "unit": "tokens/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
@@ -341,6 +514,19 @@ def main():
         return
 
     world, rank, local, dist, torch = dist_setup(args.gpus)
+    if "ring" in cfg:
+        line = run_bounded(args, cfg, world, rank, local, dist, torch)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            got = cpu_reference_ring_rate(cfg)
+            if got:
+                rate, cores, sample, kind = got
+                line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
+                                        "sample": sample}
+        if rank == 0:
+            print(json.dumps(line))
+        if dist:
+            dist.destroy_process_group()
+        return
     line = run_b200(args, cfg, world, rank, local, dist, torch)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, sample, kind, ref_logits = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)

@@ -1143,13 +1143,17 @@ int qwen_b200_trace_read(QwenB200Runner *r, unsigned long long *host, size_t cou
 
 float qwen_b200_time_stage(QwenB200Runner *r, int stage, int layer, int position, int reps) {
     if (!r || stage < 0 || stage > 5 || layer < 0 || layer >= r->d->s.layers || reps < 1 ||
-        !valid_token(r, 0, position) || (stage == 1 && !has_dense(r, layer)))
+        !valid_token(r, 0, position) || (stage == 1 && !has_dense(r, layer) && !r->ring_on))
         return -1.f;
     const bool bf16 = r->d->dtype == 2;
     auto once = [&](bool pdl) {
         switch (stage) {
             case 0: bf16 ? launch_qkv<uint16_t>(r, layer, pdl) : launch_qkv<float>(r, layer, pdl); break;
-            case 1: launch_attention(r, layer, pdl); break;
+            case 1:
+                // A ring layer re-encodes the session's current rows into the last token's write slot.
+                if (has_dense(r, layer)) launch_attention(r, layer, pdl);
+                else launch_ring_attention(r, layer, r->b.q, r->b.k, r->b.v, r->b.attention, pdl);
+                break;
             case 2: bf16 ? launch_oproj<uint16_t>(r, layer, pdl) : launch_oproj<float>(r, layer, pdl); break;
             case 3: bf16 ? launch_gateup<uint16_t>(r, layer, pdl) : launch_gateup<float>(r, layer, pdl); break;
             case 4: bf16 ? launch_down<uint16_t>(r, layer, pdl) : launch_down<float>(r, layer, pdl); break;

@@ -143,7 +143,9 @@ void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int writ
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Measurement aid: mean device time (ms, CUDA events) of one standalone launch
  * of fused stage `stage` of `layer` (0 q/k/v, 1 attention, 2 O projection,
- * 3 gate/up, 4 down, 5 readout) at `position`, over `reps` launches. */
+ * 3 gate/up, 4 down, 5 readout) at `position`, over `reps` launches. On a ring
+ * layer, stage 1 is the ring attention of the last token's step (it rewrites
+ * that token's row of the layer with the session's current K/V). */
 float qwen_b200_time_stage(QwenB200Runner *, int stage, int layer, int position, int reps);
 
 /* Timeline trace for performance work: with tracing on, every launch of a token
