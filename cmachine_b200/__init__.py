@@ -133,6 +133,7 @@ def _declare(L, strict: bool = True):
         "qwen_reset": (c_int, [P]), "qwen_port_name": (ctypes.c_char_p, [c_int]),
         "qwen_generate": (c_int, [P, c_int, POINTER(c_int)]),
         "qwen_complete_token": (c_int, [P]),
+        "qwen_push_batch": (c_int, [P, c_int, P]),
         # include/qwen_b200.h
         "qwen_b200_decoder_weight_bytes": (c_size_t, [P]),
         "qwen_b200_launches_per_token": (c_int, [P]),
@@ -149,6 +150,12 @@ def _declare(L, strict: bool = True):
         "qwen_b200_register_matrix": (None, [P, c_int, c_int, c_int]),
         "qwen_b200_complete": (c_int, [P, POINTER(Top2)]), "qwen_b200_can_complete": (c_int, [P]),
         "qwen_b200_ring_rows": (None, [P, c_int, c_int, P, c_int, c_int, c_int]),
+        "qwen_b200_batch_create": (P, [P]), "qwen_b200_batch_free": (None, [P]), "qwen_b200_batch_max": (c_int, []),
+        "qwen_b200_batch_launches_per_step": (c_int, [P]),
+        "qwen_b200_batch_step": (c_int, [P, c_int, P, P, P, P]),
+        "qwen_b200_batch_enqueue": (c_int, [P, c_int, P, P, P, c_int]),
+        "qwen_b200_batch_read": (c_int, [P, c_int, c_int, P, P]),
+        "qwen_b200_batch_matmul": (c_int, [P, c_int, c_int, P, c_int, P, c_int]),
         "qwen_b200_unregister_matrix": (None, [P]),
         # host/session_view.c
         "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),
@@ -214,6 +221,20 @@ class Model:
         if self._live:
             self.L.qwen_model_free(self.handle)
             self._live = False
+
+
+class BatchSession(Structure):
+    """QwenB200BatchSession (include/qwen_b200.h)."""
+    _fields_ = [("keys", c_void_p), ("values", c_void_p), ("capacity", c_int), ("logits", c_void_p), ("x", c_void_p)]
+
+
+def push_batch(sessions, tokens) -> int:
+    """qwen_push_batch: one batched step, session i takes tokens[i]."""
+    L = sessions[0].L
+    n = len(sessions)
+    handles = (c_void_p * n)(*[s.handle.value for s in sessions])
+    toks = (c_int * n)(*tokens)
+    return L.qwen_push_batch(ctypes.cast(handles, c_void_p), n, ctypes.cast(toks, c_void_p))
 
 
 class Checkpoint:

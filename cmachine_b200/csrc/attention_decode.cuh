@@ -248,60 +248,19 @@ struct ByteRows {
     __device__ __forceinline__ float bias(int t) const { return (weighted && t >= na && t < na + nm) ? bias_v : 0.f; }
 };
 
+// One warp's flash-decoding over rows [r0, r1) of `rows` for the G query
+// heads whose 4 dimensions per lane are in q4: four rows per step (the next
+// step's rows loaded ahead), a reduce-scatter butterfly leaving lane
+// (row i = lane / 8, head g = lane % 8) with one score, the running max and
+// sum of head g kept in the lanes with lane % 8 == g. Returns the warp's state
+// in (m[G], l[G], acc[G]) (every lane holds m and l of every head).
 template <int G, class Rows>
-__global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
-    Rows rows, const float *__restrict__ q, float inv_sqrt_dim, float *__restrict__ part,
-    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace) {
-    static_assert(G <= 8, "query heads per KV head are padded to eight");
+__device__ __forceinline__ void flash_rows(const Rows &rows, int r0, int r1, const float4 (&q4)[G], int lane,
+                                           float inv_sqrt_dim, float (&m)[G], float (&l)[G], float4 (&acc)[G]) {
     constexpr int GP = 8;       // padded heads: 4 rows x 8 heads = 32 scores, one per lane
     constexpr int kStep = 4;    // rows per step
-    __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
-    __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
-    __shared__ __align__(16) float cta_part[kAttnPartialFloats];
-    __shared__ int last_s;
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int kvh = blockIdx.y, rank = (int)cluster.block_rank(), cid = blockIdx.x / kCluster;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
-    if (mark && tid == 0) mark[0] = attn_clock();
-    // The token state (position, ring step) is written before a token's first
-    // kernel and the cache rows below the newest were written by earlier
-    // tokens, so the row split and an L2 prefetch of those rows need not wait
-    // for the q/k/v kernel; q and this token's K/V are read after
-    // griddepcontrol.wait.
-    rows.bind(kvh);
-    const int L = rows.length();
-    const int clusters = (int)(gridDim.x / kCluster);
-    const bool multi = L > kSingleClusterRows && clusters > 1;
-    if (!multi && cid > 0) {  // whole clusters leave together
-        pdl_trigger();
-        if (mark && tid == 0) mark[0] = 0ull;  // no work: not part of the timeline
-        return;
-    }
-    const int ctas = multi ? clusters * kCluster : kCluster, cta = multi ? cid * kCluster + rank : rank;
-    const int chunk = (L + ctas - 1) / ctas;
-    const int t0 = min(L, cta * chunk), t1 = min(L, t0 + chunk);
-    const int per_warp = (t1 - t0 + kDecodeAttnWarps - 1) / kDecodeAttnWarps;
-    const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
-    {
-        constexpr int kRowsPerPass = 32 / Rows::kLines;
-        const int limit = min(r1, rows.prefetch_limit());
-        for (int t = r0 + lane / Rows::kLines; t < limit; t += kRowsPerPass) rows.prefetch_line(t, lane % Rows::kLines);
-    }
-    pdl_wait();
-    if (mark && tid == 0) mark[1] = attn_clock();
-    pdl_trigger();
-    rows.current(lane, warp, cta);
-
-    float4 q4[G], acc[G];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        q4[g] = reinterpret_cast<const float4 *>(q + ((size_t)kvh * G + g) * kHeadDim)[lane];
-        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    // Lane (row i = lane / 8, head g = lane % 8) owns one score per step; the
-    // running max and sum of head g are kept in the lanes with lane % 8 == g.
+    for (int g = 0; g < G; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int my_row = lane >> 3, my_head = lane & 7;
     float m_run = -INFINITY, l_run = 0.f;
     float4 k4[kStep], v4[kStep], nk4[kStep], nv4[kStep];
@@ -385,12 +344,65 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
             v4[i] = nv4[i];
         }
     }
-    float m[G], l[G];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         m[g] = __shfl_sync(0xffffffffu, m_run, g);
         l[g] = __shfl_sync(0xffffffffu, l_run, g);
     }
+}
+
+template <int G, class Rows>
+__global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
+    Rows rows, const float *__restrict__ q, float inv_sqrt_dim, float *__restrict__ part,
+    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace) {
+    static_assert(G <= 8, "query heads per KV head are padded to eight");
+    __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
+    __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
+    __shared__ __align__(16) float cta_part[kAttnPartialFloats];
+    __shared__ int last_s;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int kvh = blockIdx.y, rank = (int)cluster.block_rank(), cid = blockIdx.x / kCluster;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
+    if (mark && tid == 0) mark[0] = attn_clock();
+    // The token state (position, ring step) is written before a token's first
+    // kernel and the cache rows below the newest were written by earlier
+    // tokens, so the row split and an L2 prefetch of those rows need not wait
+    // for the q/k/v kernel; q and this token's K/V are read after
+    // griddepcontrol.wait.
+    rows.bind(kvh);
+    const int L = rows.length();
+    const int clusters = (int)(gridDim.x / kCluster);
+    const bool multi = L > kSingleClusterRows && clusters > 1;
+    if (!multi && cid > 0) {  // whole clusters leave together
+        pdl_trigger();
+        if (mark && tid == 0) mark[0] = 0ull;  // no work: not part of the timeline
+        return;
+    }
+    const int ctas = multi ? clusters * kCluster : kCluster, cta = multi ? cid * kCluster + rank : rank;
+    const int chunk = (L + ctas - 1) / ctas;
+    const int t0 = min(L, cta * chunk), t1 = min(L, t0 + chunk);
+    const int per_warp = (t1 - t0 + kDecodeAttnWarps - 1) / kDecodeAttnWarps;
+    const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
+    {
+        constexpr int kRowsPerPass = 32 / Rows::kLines;
+        const int limit = min(r1, rows.prefetch_limit());
+        for (int t = r0 + lane / Rows::kLines; t < limit; t += kRowsPerPass) rows.prefetch_line(t, lane % Rows::kLines);
+    }
+    pdl_wait();
+    if (mark && tid == 0) mark[1] = attn_clock();
+    pdl_trigger();
+    rows.current(lane, warp, cta);
+
+    float4 q4[G], acc[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        q4[g] = reinterpret_cast<const float4 *>(q + ((size_t)kvh * G + g) * kHeadDim)[lane];
+        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float m[G], l[G];
+    flash_rows<G>(rows, r0, r1, q4, lane, inv_sqrt_dim, m, l, acc);
     if (mark && tid == 0) mark[2] = attn_clock();
     // This CTA's slice result into shared memory, then the cluster combine:
     // rank r folds the cluster's partials for outputs [r * kOutPer, ...).

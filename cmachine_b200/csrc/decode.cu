@@ -695,6 +695,18 @@ struct QwenB200Runner {
     QwenB200RingStep staged;    // written with the next token state
 };
 
+int tcm::decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
+                 const float **final_norm, const float **rope_den, int *dtype) {
+    if (!d) return -1;
+    *shape = d->s;
+    *layers = d->layers.data();
+    *embed = d->embed;
+    *final_norm = d->norm;
+    *rope_den = d->rope_den;
+    *dtype = d->dtype;
+    return 0;
+}
+
 namespace {
 
 void setup_attention() {

@@ -5,6 +5,8 @@
 #include "attention.cuh"
 
 struct TcmGpu;
+struct QwenB200Decoder;
+#include "../../include/qwen_b200.h"
 
 namespace tcm {
 
@@ -29,5 +31,9 @@ const float *rope_denominators(float theta, int dim);
 // Weight registry of the residence profile: dtype of a matrix handle
 // (1 FP32, 2 BF16) or 0 when the pointer is not a registered matrix.
 int weight_dtype(const void *p);
+
+// The fused decoder's shape, tensors and tables (for the batched engine).
+int decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
+                 const float **final_norm, const float **rope_den, int *dtype);
 
 }  // namespace tcm

@@ -105,6 +105,7 @@ int qwen_model_init_seeded(QwenModel *m, const QwenB200Shape *shape, uint64_t se
 
 void qwen_model_free(QwenModel *m) {
     if (!m) return;
+    qwen_b200_batch_free(m->batch);
     qwen_b200_decoder_free(m->fused);
     for (unsigned i = 0; i < m->allocation_count; i++) {
         if (m->matrix_dtype == 2) qwen_b200_unregister_matrix(m->allocations[i]);
@@ -388,6 +389,50 @@ int qwen_generate(QwenSession *s, int n, int *ids) {
     free(tops);
     free(lineages);
     return 0;
+}
+
+int qwen_push_batch(QwenSession **ss, int n, const int *tokens) {
+    if (!ss || !tokens || n < 1 || n > qwen_b200_batch_max()) return -1;
+    QwenModel *m = (QwenModel *)ss[0]->model;
+    if (!m->fused || m->matrix_dtype != 2) return -1;
+    for (int i = 0; i < n; i++) {
+        QwenSession *s = ss[i];
+        if (s->model != m || !fused_token_ok(s) || begin_guards(s, tokens[i]) || s->position >= 8192) return -1;
+        for (int j = 0; j < i; j++)
+            if (ss[j] == s) return -1;
+    }
+    if (!m->batch) m->batch = qwen_b200_batch_create(m->fused);
+    if (!m->batch) return -1;
+    QwenB200BatchSession *bs = malloc((size_t)n * sizeof(*bs));
+    int *positions = malloc((size_t)n * sizeof(int));
+    uint64_t *lineages = malloc((size_t)n * sizeof(uint64_t));
+    TcmTop2 *tops = malloc((size_t)n * sizeof(TcmTop2));
+    int status = -1;
+    if (!bs || !positions || !lineages || !tops) goto done;
+    for (int i = 0; i < n; i++) {
+        QwenSession *s = ss[i];
+        QwenB200BatchSession b = {s->keys, s->values, s->capacity, s->logits, s->x};
+        bs[i] = b;
+        positions[i] = s->position;
+    }
+    status = qwen_b200_batch_step(m->batch, n, bs, tokens, positions, tops);
+    if (status == -3) { fprintf(stderr, "non-finite Qwen logits\n"); exit(2); }
+    if (status) { status = -1; goto done; }
+    for (int i = 0; i < n; i++)
+        if (take_id(&next_lineage_id, &lineages[i])) { status = -1; goto done; }
+    for (int i = 0; i < n; i++) {
+        QwenSession *s = ss[i];
+        snapshot(s, &s->token_parent);
+        s->current_token = tokens[i];
+        s->top = tops[i];
+        finish_bookkeeping(s, lineages[i]);
+    }
+done:
+    free(bs);
+    free(positions);
+    free(lineages);
+    free(tops);
+    return status;
 }
 
 /* ------------------------------------------------------------------ checkpoints */

@@ -48,6 +48,7 @@ typedef struct {
     size_t weight_bytes;
     QwenB200Decoder *fused;
     int matrix_dtype;
+    QwenB200Batch *batch;  /* the batched engine, created on the first qwen_push_batch */
 } QwenModel;
 
 /* src/qwen.h:46-52 */
@@ -145,6 +146,16 @@ int qwen_generate(QwenSession *, int n, int *ids);
  * -81 when a layer encoded a non-finite K/V row into its byte cache (the token
  * is left open for abort, as after a failed layer). */
 int qwen_complete_token(QwenSession *);
+
+/* B200 addition: qwen_push for n sessions of one model in one batched step
+ * (include/qwen_b200.h, tcgen05 GEMMs): session i takes tokens[i]; every
+ * session's K/V, logits, top-2, pending token, position and lineage end as n
+ * separate qwen_push calls would leave them. All sessions must be distinct,
+ * belong to a BF16 model with the fused decoder, keep their K/V in the session
+ * (no cache callbacks), have no port observed at their position, and pass
+ * qwen_push's guards; n <= 64, positions < 8192. Returns 0, or -1 with nothing
+ * changed. */
+int qwen_push_batch(QwenSession **sessions, int n, const int *tokens);
 
 #ifdef __cplusplus
 }

@@ -139,6 +139,42 @@ int qwen_b200_can_complete(const QwenB200Runner *);
  * saved rows back. Device pointers; sample_slot -1 skips the sample row. */
 void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int write_slot, int sample_slot, int mode);
 
+/* ---- Batched decode of independent sessions (BF16 weights) ----
+ * One step decodes one token for each of n <= qwen_b200_batch_max() sessions
+ * sharing the decoder's weights: the q/k/v, O, gate/up, down and vocabulary
+ * projections run as tcgen05 tensor-core GEMMs (BF16 weights x activations
+ * split into two BF16 halves, FP32 accumulation in tensor memory), attention
+ * runs per session over its own FP32 K/V. Requires a BF16 decoder of the
+ * Qwen2.5-1.5B geometry; returns NULL otherwise. */
+typedef struct QwenB200Batch QwenB200Batch;
+/* Session i of a step: its K/V slabs ([layer][2][capacity][128] FP32, the
+ * session layout of include/qwen.h), capacity, and its logits and x buffers,
+ * which the step overwrites as a single-session token would. */
+typedef struct {
+    float *keys, *values;
+    int capacity;
+    float *logits, *x;
+} QwenB200BatchSession;
+QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *);
+void qwen_b200_batch_free(QwenB200Batch *);
+int qwen_b200_batch_max(void);
+int qwen_b200_batch_launches_per_step(const QwenB200Batch *);
+/* One step: session i takes tokens[i] at positions[i] (position < 8192); tops[i]
+ * receives its top-2. 0, -1 invalid arguments (nothing ran), -3 non-finite
+ * logits, -4 a pipeline wait ran out. */
+int qwen_b200_batch_step(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                         const int *positions, TcmTop2 *tops);
+/* `steps` chained greedy steps (the device feeds every session's top-1 back and
+ * advances its position) without waiting; qwen_b200_batch_read then returns the
+ * last step's tops and, if history is set, history[t * n + i] for every step. */
+int qwen_b200_batch_enqueue(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                            const int *positions, int steps);
+int qwen_b200_batch_read(QwenB200Batch *, int n, int steps, TcmTop2 *tops, TcmTop2 *history);
+/* y[i][r] = sum_k W[r][k] x[i][k] on the tensor cores for a BF16 matrix W
+ * (rows a multiple of 128, in a multiple of 64) and n <= 64 FP32 rows x, with
+ * `splits` K-splits. Synchronous; 0, -1 invalid, -4 wait ran out. */
+int qwen_b200_batch_matmul(const void *w, int rows, int in, const float *x, int n, float *y, int splits);
+
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Measurement aid: mean device time (ms, CUDA events) of one standalone launch
