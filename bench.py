@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import argparse
 import json
+from ctypes import c_void_p
 import os
 import statistics
 import subprocess
@@ -54,6 +55,11 @@ CONFIGS = {
     # and one injected layer failure with recovery per 1,024 tokens.
     "bf16-bounded": dict(layers=28, profile=2, ring=(64, 1024, 1024), logical=32768, prefill=2200,
                          sessions=2, mark_every=256, fail_every=1024),
+    # Batched decode: full Qwen2.5-1.5B, source-BF16 weights, 64 independent
+    # sessions per GPU with contexts drawn uniformly from 128..8192, greedy steps
+    # in segments of 64 with a checkpoint at each segment start and a rollback
+    # after every second segment; projections on the tcgen05 tensor cores.
+    "bf16-batch64": dict(layers=28, profile=2, batch=64, ctx=(128, 8192), segment=64),
 }
 
 
@@ -356,6 +362,130 @@ def run_bounded(args, cfg, world, rank, local, dist, torch):
     }
 
 
+def run_batched(args, cfg, world, rank, local, dist, torch):
+    """64 sessions per GPU through the batched tensor-core engine."""
+    import ctypes
+    import numpy as np
+    import cmachine_b200 as cm
+    L = cm.lib()
+    L.qwen_b200_set_device(local)
+    shape = cm.qwen_shape(cfg["layers"], 9216)
+    model = cm.Model(shape, 2026 + rank, cm.BENCH_LAW, cfg["profile"])
+    n, seg = cfg["batch"], cfg["segment"]
+    steps = max(seg, (args.steps // seg) * seg)
+    rng = np.random.default_rng(11 + rank)
+    lengths = [int(v) for v in rng.integers(cfg["ctx"][0], cfg["ctx"][1] + 1, n)]
+    sessions = []
+    for i, ln in enumerate(lengths):
+        s = cm.Session(model, ln + steps // 2 + seg + max(args.warmup, 3) + 2)
+        v = s.view()
+        count = shape.layers * shape.kvheads * v.capacity * shape.head
+        # The context's K/V rows: seeded synthetic values of the decoder's K/V
+        # scale (the decode steps themselves are computed exactly).
+        L.qwen_b200_seeded_fill(c_void_p(v.keys), 1, 4242 + rank, 100000 + 2 * i, count, 0.0, 0.8)
+        L.qwen_b200_seeded_fill(c_void_p(v.values), 1, 4242 + rank, 100001 + 2 * i, count, 0.0, 0.8)
+        assert L.qwen_b200_session_set_cursor(s.handle, ln, int(rng.integers(0, shape.vocab))) == 0
+        sessions.append(s)
+    L.gpu_sync()
+    batch = L.qwen_b200_batch_create(L.qwen_b200_model_decoder(model.handle))
+    assert batch
+    views = [s.view() for s in sessions]
+    bs = (cm.BatchSession * n)(*[cm.BatchSession(v.keys, v.values, v.capacity, v.logits, v.x) for v in views])
+    pos = [v.position for v in views]
+    tok = [v.pending for v in views]
+    tops = (cm.Top2 * n)()
+
+    def segment(k, advance):
+        nonlocal pos, tok
+        cp, ct = (ctypes.c_int * n)(*pos), (ctypes.c_int * n)(*tok)
+        assert L.qwen_b200_batch_enqueue(batch, n, bs, ct, cp, k) == 0
+        assert L.qwen_b200_batch_read(batch, n, k, tops, None) == 0
+        if advance:  # keep the segment; otherwise roll back to its checkpoint
+            pos = [p + k for p in pos]
+            tok = [tops[i].first for i in range(n)]
+
+    segment(max(args.warmup, 3), False)
+    barrier(dist, torch)
+    with ClockSampler(local) as clocks:
+        L.qwen_b200_mark(0)
+        for c in range(steps // seg):
+            segment(seg, c % 2 == 0)
+        L.qwen_b200_mark(1)
+        L.gpu_sync()
+        device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    barrier(dist, torch)
+    device_ms = max_over_ranks(device_ms, dist, torch)
+    mean_pos = sum(pos) / n
+    # End to end through qwen_push_batch with session checkpoints.
+    e2e_steps = min(steps, 2 * seg)
+    handles = sessions
+    ck = [s.checkpoint() for s in handles]
+    assert all(st == 0 for st, _ in ck)
+    barrier(dist, torch)
+    t0 = time.perf_counter()
+    for c in range(e2e_steps // seg):
+        for _ in range(seg):
+            assert cm.push_batch(handles, [s.pending for s in handles]) == 0
+        if c % 2 == 0:
+            for s, (_, cp) in zip(handles, ck):
+                assert s.restore(cp) == 0
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, dist, torch)
+    barrier(dist, torch)
+
+    # Stage times of layer 0 at the current cursors; the roofline is the
+    # attention kernel's (the step's dominant bytes) and the tensor pipe's.
+    cp, ct = (ctypes.c_int * n)(*pos), (ctypes.c_int * n)(*tok)
+    names = ["qkv_gemm", "attention", "o_gemm", "gateup_gemm", "down_gemm", "vocab_gemm", "rmsnorm"]
+    stage = {nm: L.qwen_b200_batch_time_stage(batch, n, bs, ct, cp, i, 0, 10) for i, nm in enumerate(names)}
+    peak, peak_kind = measured_peaks()
+    attn_bytes = sum((p + 1) * shape.kvheads * shape.head * 4 * 2 for p in pos)
+    attn_gbs = attn_bytes / (stage["attention"] * 1e-3) / 1e9
+    kv_step = sum((p + 1) for p in pos) * 57344  # K and V of every layer, once a step
+    weight_bytes = model.weight_bytes
+    step_bytes = weight_bytes + kv_step
+    ms_per_step = device_ms / steps
+    gemm_flops = 2 * 2 * 1543569408 * n  # hi and lo halves: two MMAs per product
+    layer_gemm_ms = stage["qkv_gemm"] + stage["o_gemm"] + stage["gateup_gemm"] + stage["down_gemm"]
+    tflops = (gemm_flops - 2 * 2 * shape.vocab * shape.hidden * n) / shape.layers / (layer_gemm_ms * 1e-3) / 1e12
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tc_peak = float(pk.get("bf16_tflops", 1590.0))
+    gateup_bytes = 2 * shape.intermediate * shape.hidden * 2
+    L.qwen_b200_batch_free(batch)
+    for s in sessions:
+        s.free()
+    model.free()
+    tokens_total = steps * n * world
+    return {
+        "metric": METRIC, "value": round(tokens_total / (device_ms * 1e-3), 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16-weights/f32",
+        "data": "synthetic",
+        "config": {"workload": "qwen2.5-1.5b-bf16-batch64", "layers": shape.layers, "batch": n,
+                   "sessions_total": n * world, "context": "uniform 128..8192 per session (seeded)",
+                   "mean_position": round(mean_pos, 1), "segment": seg,
+                   "checkpoints": "every segment; rollback after every second segment",
+                   "kv_prefill": "context K/V rows are seeded synthetic values; decode steps exact",
+                   "parallelism": f"replicas{world}", "weights": "seeded N(0,0.02) random init",
+                   "l2": "inputs larger than L2 (weights and K/V stream from HBM every step)"},
+        "e2e": {"value": round(e2e_steps * n * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * 16},
+        "gpu_launches": (shape.layers * 7 + 4) * (steps + max(args.warmup, 3)),
+        "roofline": {"bound": "hbm", "kernel": "batch_attn_kernel (64 sessions x 2 KV heads, split-K flash decoding)",
+                     "achieved": round(attn_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(attn_gbs / peak, 4),
+                     "peak_source": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": int(attn_bytes),
+                     "launch_ms": round(stage["attention"], 5)},
+        "tensor_roofline": {"bound": "tensor", "kernels": "tc_gemm_kernel (q/k/v, O, gate/up, down of one layer)",
+                            "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                            "frac": round(tflops / tc_peak, 4),
+                            "note": "two BF16 MMAs per product (activation hi and lo halves); the GEMMs are HBM-bound",
+                            "gateup_hbm_gbs": round(gateup_bytes / (stage["gateup_gemm"] * 1e-3) / 1e9, 1)},
+        "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
+                          "frac": round(step_bytes / (ms_per_step * 1e6) / peak, 4)},
+        "stage_ms_layer0": {k: round(v, 5) for k, v in stage.items()},
+        "clocks": clocks.summary(),
+    }
+
+
 def gpu_dlogit(layers: int, profile: int, ref_logits):
     """max |delta logit| of the GPU path on the CPU sample's first thread."""
     import numpy as np
@@ -514,6 +644,18 @@ def main():
         return
 
     world, rank, local, dist, torch = dist_setup(args.gpus)
+    if "batch" in cfg:
+        line = run_batched(args, cfg, world, rank, local, dist, torch)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], True)
+            line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
+                                    "sample": sample + "; at these sessions' contexts the reference's attention adds "
+                                              "about a quarter to each token's arithmetic"}
+        if rank == 0:
+            print(json.dumps(line))
+        if dist:
+            dist.destroy_process_group()
+        return
     if "ring" in cfg:
         line = run_bounded(args, cfg, world, rank, local, dist, torch)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

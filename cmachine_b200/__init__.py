@@ -156,6 +156,12 @@ def _declare(L, strict: bool = True):
         "qwen_b200_batch_enqueue": (c_int, [P, c_int, P, P, P, c_int]),
         "qwen_b200_batch_read": (c_int, [P, c_int, c_int, P, P]),
         "qwen_b200_batch_matmul": (c_int, [P, c_int, c_int, P, c_int, P, c_int]),
+        "qwen_b200_batch_time_stage": (c_float, [P, c_int, P, P, P, c_int, c_int, c_int]),
+        "qwen_b200_batch_trace_stage": (c_int, [P, c_int, P, P, P, c_int, c_int, P, c_int]),
+        "qwen_b200_batch_tune": (c_int, [P, c_int, c_int]),
+        "qwen_b200_batch_cluster_capacity": (c_int, [c_int]),
+        "qwen_b200_batch_clusters": (c_int, [P, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
+        "qwen_b200_session_set_cursor": (c_int, [P, c_int, c_int]),
         "qwen_b200_unregister_matrix": (None, [P]),
         # host/session_view.c
         "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),

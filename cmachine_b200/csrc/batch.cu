@@ -24,6 +24,7 @@
 #include "attention.cuh"
 #include "attention_decode.cuh"
 #include "tc_gemm.cuh"
+#include "stream.cuh"
 #include "kernels.h"
 #include "../../include/qwen_b200.h"
 #include "../../include/tcm_seeded.h"
@@ -38,7 +39,7 @@ namespace {
 constexpr int kBN = 64;             // sessions per step (the tensor-core tile's N)
 constexpr int kHd = 1536, kFf = 8960;
 constexpr int kAttnChunk = 256;     // cache rows per attention CTA
-constexpr int kAttnSplitMax = 32;   // up to 8192 cached rows
+constexpr int kAttnSplitMax = 36;   // up to 9216 cached rows
 constexpr int kBatchLogCap = 256;   // steps of top-2 kept for chained decode
 
 // Device-resident batch state: the host writes it before a step; the top-2
@@ -111,6 +112,18 @@ __global__ void __launch_bounds__(256) batch_rms_kernel(RmsArgs a) {
 // q/k/v: tiles 0..11 are the 12 query heads, 12..13 the K heads, 14..15 the V
 // heads; a head is exactly one 128-row tile, so RoPE pairs (d, d + 64) meet in
 // the tile. The rotation repeats the single-session kernel's arithmetic.
+// Per-session metadata the epilogues read, staged once per CTA.
+struct SessionMeta {
+    float *keys, *values, *logits;
+    int position, capacity;
+};
+__device__ __forceinline__ void stage_meta(const BatchState *st, unsigned char *scratch, int e) {
+    SessionMeta *m = reinterpret_cast<SessionMeta *>(scratch);
+    for (int n = e; n < st->n; n += 128)
+        m[n] = SessionMeta{st->keys[n], st->values[n], st->logits[n], st->position[n], st->capacity[n]};
+}
+static_assert(sizeof(SessionMeta) * kBN <= 2048, "epilogue scratch");
+
 struct EpiQkv {
     BatchState *st;
     const float *bq, *bk, *bv, *rope_den;
@@ -120,16 +133,21 @@ struct EpiQkv {
         const int m = t < 12 ? 0 : (t < 14 ? 1 : 2), r = (t < 12 ? t : (t < 14 ? t - 12 : t - 14)) * 128;
         return TcRows{m, r, m, r + 64};
     }
-    template <int NP> __device__ void store(int t, const float (*tile)[NP], int e) const {
+    __device__ void init(unsigned char *scratch, int e) const { stage_meta(st, scratch, e); }
+    // Row pairs (d, d + 64) for d in [p0, p1), every session; consecutive threads
+    // take consecutive d.
+    template <int NP>
+    __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *scratch) const {
+        const SessionMeta *meta = reinterpret_cast<const SessionMeta *>(scratch);
         const int kind = t < 12 ? 0 : (t < 14 ? 1 : 2), head = t < 12 ? t : (t < 14 ? t - 12 : t - 14);
         const float *bias = (kind == 0 ? bq : kind == 1 ? bk : bv) + head * 128;
-        const int n_active = st->n;
-        for (int idx = e; idx < 64 * n_active; idx += 128) {
-            const int d = idx & 63, n = idx >> 6;
+        const int np = p1 - p0, n_active = st->n;
+        for (int idx = e; idx < np * n_active; idx += 128) {
+            const int d = p0 + idx % np, n = idx / np;
             float y0 = __fadd_rn(tile[d][n], bias[d]), y1 = __fadd_rn(tile[d + 64][n], bias[d + 64]);
-            const int pos = st->position[n];
+            const SessionMeta &mt = meta[n];
             if (kind < 2) {
-                const float angle = __fdiv_rn((float)pos, rope_den[d]);
+                const float angle = __fdiv_rn((float)mt.position, rope_den[d]);
                 float sn, cs;
                 sincosf(angle, &sn, &cs);
                 const float r0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
@@ -141,26 +159,45 @@ struct EpiQkv {
                 q[(size_t)n * kHd + head * 128 + d] = y0;
                 q[(size_t)n * kHd + head * 128 + d + 64] = y1;
             } else {
-                const int cap = st->capacity[n];
-                float *cache = (kind == 1 ? st->keys[n] : st->values[n]) + ((size_t)layer * 2 + head) * cap * 128 +
-                               (size_t)pos * 128;
+                float *cache = (kind == 1 ? mt.keys : mt.values) + ((size_t)layer * 2 + head) * mt.capacity * 128 +
+                               (size_t)mt.position * 128;
                 cache[d] = y0;
                 cache[d + 64] = y1;
             }
         }
     }
 };
+// Rows {p, p + 64 : p in [p0, p1)} of an output tile as (row, session) items:
+// item i is row rows[i % 2np], session i / 2np.
+__device__ __forceinline__ int pair_row(int i, int p0, int np) {
+    const int k = i % (2 * np);
+    return k < np ? p0 + k : 64 + p0 + (k - np);
+}
 // x += D (the O and down projections): tile rows are output rows t*128 ...
+// The loads of a group of items are issued together, then the sums stored.
 struct EpiResid {
     BatchState *st;
     float *x;
     __device__ TcRows a_rows(int t) const { return TcRows{0, t * 128, 0, t * 128 + 64}; }
-    template <int NP> __device__ void store(int t, const float (*tile)[NP], int e) const {
-        const int n_active = st->n;
-        for (int idx = e; idx < 128 * n_active; idx += 128) {
-            const int r = idx & 127, n = idx >> 7;
-            float *p = x + (size_t)n * kHd + t * 128 + r;
-            *p = __fadd_rn(*p, tile[r][n]);
+    __device__ void init(unsigned char *, int) const {}
+    template <int NP>
+    __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *) const {
+        const int np = p1 - p0, total = 2 * np * st->n;
+        for (int base = 0; base < total; base += 128 * 8) {
+            float xv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int i = base + e + 128 * j;
+                xv[j] = i < total ? x[(size_t)(i / (2 * np)) * kHd + t * 128 + pair_row(i, p0, np)] : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int i = base + e + 128 * j;
+                if (i < total) {
+                    const int r = pair_row(i, p0, np), n = i / (2 * np);
+                    x[(size_t)n * kHd + t * 128 + r] = __fadd_rn(xv[j], tile[r][n]);
+                }
+            }
         }
     }
 };
@@ -170,10 +207,12 @@ struct EpiSwiglu {
     BatchState *st;
     uint16_t *hh, *hl;   // [kBN][8960]
     __device__ TcRows a_rows(int t) const { return TcRows{0, t * 64, 1, t * 64}; }
-    template <int NP> __device__ void store(int t, const float (*tile)[NP], int e) const {
-        const int n_active = st->n;
-        for (int idx = e; idx < 64 * n_active; idx += 128) {
-            const int i = idx & 63, n = idx >> 6;
+    __device__ void init(unsigned char *, int) const {}
+    template <int NP>
+    __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *) const {
+        const int np = p1 - p0, n_active = st->n;
+        for (int idx = e; idx < np * n_active; idx += 128) {
+            const int i = p0 + idx % np, n = idx / np;
             const float g = tile[i][n], u = tile[i + 64][n];
             const float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
             uint16_t hi, lo;
@@ -183,30 +222,18 @@ struct EpiSwiglu {
         }
     }
 };
-// Logits to each session's buffer, and the tile's top-2 per session.
+// Logits to each session's buffer (the top-2 is taken from them afterwards).
 struct EpiLogits {
     BatchState *st;
-    Top2 *part;   // [tiles][kBN]
     __device__ TcRows a_rows(int t) const { return TcRows{0, t * 128, 0, t * 128 + 64}; }
-    template <int NP> __device__ void store(int t, const float (*tile)[NP], int e) const {
-        const int n_active = st->n;
-        for (int idx = e; idx < 128 * n_active; idx += 128) {
-            const int r = idx & 127, n = idx >> 7;
-            st->logits[n][t * 128 + r] = tile[r][n];
-        }
-        const int warp = e >> 5, lane = e & 31;
-        for (int n = warp; n < n_active; n += 4) {
-            Top2 z = top2_empty();
-            bool bad = false;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float v = tile[lane + 32 * j][n];
-                bad |= !isfinite(v);
-                top2_insert(z, v, t * 128 + lane + 32 * j);
-            }
-            top2_merge_warp(z);
-            if (__any_sync(0xffffffffu, bad) && lane == 0) st->bad[n] = 1;
-            if (lane == 0) part[(size_t)t * kBN + n] = z;
+    __device__ void init(unsigned char *scratch, int e) const { stage_meta(st, scratch, e); }
+    template <int NP>
+    __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *scratch) const {
+        const SessionMeta *meta = reinterpret_cast<const SessionMeta *>(scratch);
+        const int np = p1 - p0, total = 2 * np * st->n;
+        for (int i = e; i < total; i += 128) {
+            const int r = pair_row(i, p0, np), n = i / (2 * np);
+            meta[n].logits[t * 128 + r] = tile[r][n];
         }
     }
 };
@@ -216,9 +243,12 @@ struct EpiStore {
     float *y;
     int rows, n;
     __device__ TcRows a_rows(int t) const { return TcRows{0, t * 128, 0, t * 128 + 64}; }
-    template <int NP> __device__ void store(int t, const float (*tile)[NP], int e) const {
-        for (int idx = e; idx < 128 * n; idx += 128) {
-            const int r = idx & 127, c = idx >> 7;
+    __device__ void init(unsigned char *, int) const {}
+    template <int NP>
+    __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *) const {
+        const int np = p1 - p0, total = 2 * np * n;
+        for (int i = e; i < total; i += 128) {
+            const int r = pair_row(i, p0, np), c = i / (2 * np);
             y[(size_t)c * rows + t * 128 + r] = tile[r][c];
         }
     }
@@ -233,94 +263,350 @@ __global__ void split_rows_kernel(const float *x, uint16_t *hi, uint16_t *lo, si
 }
 
 // ---------------------------------------------------------------- attention
+// Work items are (session n, KV head h, chunk c of kAttnItemRows cache rows),
+// numbered session by session; a persistent grid of one CTA per SM takes items
+// blockIdx.x, blockIdx.x + gridDim.x, ... Per CTA one producer thread streams
+// each chunk's K and V rows (contiguous in the session's [head][capacity][128]
+// slab) into a ring of shared-memory stages with cp.async.bulk, 32 rows of K
+// and 32 of V a stage; every consumer warp takes four rows of each stage as
+// one flash-decoding step. At the end of an item the eight warps' states merge
+// into a partial in global memory; the last CTA of the (session, head) to
+// arrive folds the partials in chunk order and writes the output rows as BF16
+// hi/lo for the O projection.
+constexpr int kAttnRowsPerStage = 32;                  // 8 warps x 4 rows
+constexpr int kAttnStageBytes = 2 * kAttnRowsPerStage * kHeadDim * 4;  // K and V: 32 KB
+constexpr int kAttnRingStages = 6;
+constexpr int kAttnItemRowsMin = 256;   // item sizes are multiples of 32 rows in [256, 2048]
+constexpr int kAttnItemMax = (kAttnSplitMax * kAttnChunk) / kAttnItemRowsMin;  // chunks per (session, head)
+constexpr size_t kAttnSmem = ring_smem_bytes(kAttnRingStages, kAttnStageBytes);
+
 struct AttnArgs {
     BatchState *st;
     const float *q;        // [kBN][1536]
     int layer;
     float inv_sqrt_dim;
-    float *part;           // [kBN][2][kAttnSplitMax][kAttnPartialFloats]
+    float *part;           // [kBN][2][kAttnItemMax][kAttnPartialFloats]
     unsigned *counters;    // [kBN][2]
     uint16_t *oh, *ol;     // [kBN][1536]
+    unsigned long long *trace;  // per CTA: 0 entry, 1 consumers released, 2 first stage ready, 3 last item done
+    unsigned *work;        // [0] next item, [1] CTAs done (reset by the last CTA)
+    int item_rows;         // cache rows per work item
 };
-__global__ void __launch_bounds__(kDecodeAttnThreads, 2) batch_attn_kernel(AttnArgs a) {
-    constexpr int G = 6;
-    __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
-    __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
-    __shared__ int last_s;
-    const int s = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    pdl_trigger();
-    // The state block is written before the step: the split needs no wait.
-    if (n >= a.st->n) return;
-    const int L = a.st->position[n] + 1, splits = (L + kAttnChunk - 1) / kAttnChunk;
-    if (s >= splits) return;
-    const int cap = a.st->capacity[n];
-    DenseRows rows = {};
-    rows.keys = a.st->keys[n] + (size_t)a.layer * 2 * cap * kHeadDim;
-    rows.values = a.st->values[n] + (size_t)a.layer * 2 * cap * kHeadDim;
-    rows.capacity = cap;
-    rows.position = &a.st->position[n];
-    rows.bind(h);
-    const int t0 = s * kAttnChunk, t1 = min(L, t0 + kAttnChunk);
-    const int per_warp = kAttnChunk / kDecodeAttnWarps;
-    const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
-    for (int t = r0 + (lane >> 2); t < min(r1, L - 1); t += 8) rows.prefetch_line(t, lane & 3);
-    pdl_wait();
-    float4 q4[G], acc[G];
+
+// One flash-decoding step of a warp over `nrows` (<= 4) rows held in k4/v4 for
+// three query heads (q4): the 4 rows x 4 padded heads = 16 partial dots are
+// reduced by a reduce-scatter over lane bits 3..0 and one fold over bit 4, so
+// lane (row (lane & 15) / 4, head lane & 3) holds a full score; the running
+// max and sum of head g live in the lanes with lane & 3 == g. Scores are kept
+// in base 2 (scale = log2(e) / sqrt(128)) so the softmax uses exp2; arithmetic
+// on pairs of dimensions uses the packed FP32x2 FMA.
+__device__ __forceinline__ void flash_step3(const float4 (&q4)[3], const float4 (&k4)[4], const float4 (&v4)[4],
+                                            int nrows, int lane, float scale2, float &m_run, float &l_run,
+                                            float4 (&acc)[3]) {
+    float v[16];
 #pragma unroll
-    for (int g = 0; g < G; g++) q4[g] = reinterpret_cast<const float4 *>(a.q + (size_t)n * kHd + (h * G + g) * kHeadDim)[lane];
-    float m[G], l[G];
-    flash_rows<G>(rows, r0, r1, q4, lane, a.inv_sqrt_dim, m, l, acc);
-    float *hp = a.part + ((size_t)n * 2 + h) * kAttnSplitMax * kAttnPartialFloats;
-    cta_merge<G>(m, l, acc, wm, wl, wacc, hp + (size_t)s * kAttnPartialFloats, nullptr);
-    __threadfence();
-    __syncthreads();
-    unsigned *counter = &a.counters[n * 2 + h];
-    if (tid == 0) last_s = atomicAdd(counter, 1u) == (unsigned)(splits - 1);
-    __syncthreads();
-    if (!last_s) return;
-    __threadfence();
-    for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
-        const int g = o / kHeadDim, d = o % kHeadDim;
-        float M = -INFINITY;
-        for (int c = 0; c < splits; c++) M = fmaxf(M, __ldcg(hp + (size_t)c * kAttnPartialFloats + g));
-        float num = 0.f, den = 0.f;
-        for (int c = 0; c < splits; c++) {
-            const float *pc = hp + (size_t)c * kAttnPartialFloats;
-            const float mc = __ldcg(pc + g);
-            if (mc == -INFINITY) continue;
-            const float e = expf(mc - M);
-            den = fmaf(e, __ldcg(pc + kAttnMaxGroup + g), den);
-            num = fmaf(e, __ldcg(pc + 2 * kAttnMaxGroup + g * kHeadDim + d), num);
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            if (g < 3) {
+                float2 d = __fmul2_rn(make_float2(q4[g].x, q4[g].y), make_float2(k4[i].x, k4[i].y));
+                d = __ffma2_rn(make_float2(q4[g].z, q4[g].w), make_float2(k4[i].z, k4[i].w), d);
+                v[4 * i + g] = d.x + d.y;
+            } else {
+                v[4 * i + g] = 0.f;
+            }
         }
-        uint16_t hi, lo;
-        split_bf16(__fdiv_rn(num, den), hi, lo);
-        a.oh[(size_t)n * kHd + (h * G + g) * kHeadDim + d] = hi;
-        a.ol[(size_t)n * kHd + (h * G + g) * kHeadDim + d] = lo;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < o; j++) {
+            const float send = upper ? v[j] : v[j + o];
+            const float keep = upper ? v[j + o] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
     }
-    if (tid == 0) *counter = 0u;
+    const float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
+    const int my_row = (lane & 15) >> 2, my_head = lane & 3;
+    const float sc = (my_row < nrows && my_head < 3) ? dot * scale2 : -INFINITY;
+    float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    const float m_new = fmaxf(m_run, mx);
+    const float c = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+    const float p = sc == -INFINITY ? 0.f : exp2f(sc - m_new);
+    float ps = p + __shfl_xor_sync(0xffffffffu, p, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    l_run = fmaf(l_run, c, ps);
+    m_run = m_new;
+#pragma unroll
+    for (int g = 0; g < 3; g++) {
+        const float cg_ = __shfl_sync(0xffffffffu, c, g);
+        float2 lo = __fmul2_rn(make_float2(acc[g].x, acc[g].y), make_float2(cg_, cg_));
+        float2 hi = __fmul2_rn(make_float2(acc[g].z, acc[g].w), make_float2(cg_, cg_));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float pg = __shfl_sync(0xffffffffu, p, 4 * i + g);
+            lo = __ffma2_rn(make_float2(pg, pg), make_float2(v4[i].x, v4[i].y), lo);
+            hi = __ffma2_rn(make_float2(pg, pg), make_float2(v4[i].z, v4[i].w), hi);
+        }
+        acc[g] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+}
+
+// 16 consumer warps: warp w takes rows 4 (w / 2) .. + 3 of each 32-row stage for
+// query heads 3 (w % 2) .. + 2 of the KV head; one producer warp.
+constexpr int kBatchAttnWarps = 16;
+constexpr int kBatchAttnThreads = (kBatchAttnWarps + 1) * 32;
+__device__ __forceinline__ void attn_consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kBatchAttnWarps * 32) : "memory"); }
+
+__global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnArgs a) {
+    constexpr int G = 6, GH = 3;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int chunk_start[kBN + 1];   // first item of each session (prefix over sessions)
+    __shared__ int stage_item[kAttnRingStages], stage_row[kAttnRingStages];
+    __shared__ float wm[kBatchAttnWarps][GH], wl[kBatchAttnWarps][GH];
+    __shared__ __align__(16) float wacc[kBatchAttnWarps][GH][kHeadDim];
+    __shared__ int last_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    Ring ring;
+    ring.buf = smem;
+    ring.stage_bytes = kAttnStageBytes;
+    ring.stages = kAttnRingStages;
+    ring.full = reinterpret_cast<uint64_t *>(smem + (size_t)kAttnRingStages * kAttnStageBytes);
+    ring.empty = ring.full + kAttnRingStages;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kAttnRingStages; st++) {
+            mbar_init(&ring.full[st], 1);
+            mbar_init(&ring.empty[st], kBatchAttnWarps);
+        }
+        mbar_fence_init();
+    }
+    pdl_trigger();
+    if (threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 0] = global_ns();
+    // The state block is written before the step; this token's rows (position)
+    // are written by the q/k/v GEMM, so copies that include them wait for it.
+    const int n_active = a.st->n;
+    if (threadIdx.x == 0) {
+        int acc_items = 0;
+        for (int n = 0; n < n_active; n++) {
+            chunk_start[n] = acc_items;
+            acc_items += 2 * ((a.st->position[n] + a.item_rows) / a.item_rows);
+        }
+        chunk_start[n_active] = acc_items;
+    }
+    __syncthreads();
+    const int items = chunk_start[n_active];
+    auto locate = [&](int item, int &n, int &h, int &c, int &rows0, int &rows1) {
+        int lo = 0, hi = n_active - 1;  // last session with chunk_start <= item
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (chunk_start[mid] <= item) lo = mid;
+            else hi = mid - 1;
+        }
+        n = lo;
+        const int within = item - chunk_start[n], chunks = (chunk_start[n + 1] - chunk_start[n]) / 2;
+        h = within / chunks;
+        c = within % chunks;
+        const int L = a.st->position[n] + 1;
+        rows0 = c * a.item_rows;
+        rows1 = min(L, rows0 + a.item_rows);
+    };
+
+    if (warp == kBatchAttnWarps) {
+        // Producer: items come from a global counter (the first free item goes
+        // to the first free CTA), their stages into the ring; each stage carries
+        // its item and first row, and a stage with item -1 ends the stream.
+        if (lane == 0) {
+            bool waited = false, ok = true;
+            int g = 0;
+            for (;;) {
+                const int item = (int)atomicAdd(&a.work[0], 1u);
+                const bool done = item >= items;
+                int n = 0, h = 0, c = 0, r0 = 0, r1 = 1;
+                if (!done) locate(item, n, h, c, r0, r1);
+                const int cap = done ? 0 : a.st->capacity[n], last = done ? 0 : a.st->position[n];
+                const float *kb = done ? nullptr : a.st->keys[n] + ((size_t)a.layer * 2 + h) * cap * kHeadDim;
+                const float *vb = done ? nullptr : a.st->values[n] + ((size_t)a.layer * 2 + h) * cap * kHeadDim;
+                for (int t = r0; t < r1; t += kAttnRowsPerStage, g++) {
+                    const int s = g % kAttnRingStages, rows = min(kAttnRowsPerStage, r1 - t);
+                    if (g >= kAttnRingStages &&
+                        !mbar_wait(&ring.empty[s], ((g / kAttnRingStages) & 1) ^ 1, &a.st->err, kErrEmptyWait)) {
+                        ok = false;
+                        break;
+                    }
+                    stage_item[s] = done ? -1 : item;
+                    stage_row[s] = t;
+                    if (done) {
+                        mbar_arrive(&ring.full[s]);  // the end marker: no data
+                        g++;  // counted, so the drain below sees each stage's latest phase
+                        break;
+                    }
+                    if (!waited && t + rows > last) {  // this stage holds the newest row
+                        pdl_wait();
+                        waited = true;
+                    }
+                    const uint32_t bytes = (uint32_t)rows * kHeadDim * 4;
+                    mbar_expect_tx(&ring.full[s], 2 * bytes);
+                    bulk_copy_g2s(ring.stage(s), kb + (size_t)t * kHeadDim, bytes, &ring.full[s]);
+                    bulk_copy_g2s(ring.stage(s) + kAttnStageBytes / 2, vb + (size_t)t * kHeadDim, bytes, &ring.full[s]);
+                }
+                if (done || !ok) break;
+            }
+            for (int d = g > kAttnRingStages ? g - kAttnRingStages : 0; d < g; d++)
+                if (!mbar_wait(&ring.full[d % kAttnRingStages], (d / kAttnRingStages) & 1, &a.st->err, kErrDrain)) break;
+        }
+    } else {
+        pdl_wait();
+        const int tid = threadIdx.x, quad = warp >> 1, half = warp & 1;
+        const float scale2 = a.inv_sqrt_dim * 1.44269504088896340736f;  // log2(e) / sqrt(128): base-2 scores
+        if (tid == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 1] = global_ns();
+        int g = 0;
+        int cur = -1, n = 0, h = 0, c = 0, r0 = 0, r1 = 0;
+        float4 q4[GH], acc[GH];
+        float m_run = -INFINITY, l_run = 0.f;
+        for (;;) {
+            if (!mbar_wait(&ring.full[g % kAttnRingStages], (g / kAttnRingStages) & 1, &a.st->err, kErrFullWait)) break;
+            const int s = g % kAttnRingStages, item = stage_item[s], t = stage_row[s];
+            if (item < 0) break;  // end of the stream (the producer's last stage)
+            if (g == 0 && tid == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 2] = global_ns();
+            if (item != cur) {
+                cur = item;
+                locate(item, n, h, c, r0, r1);
+#pragma unroll
+                for (int gg = 0; gg < GH; gg++) {
+                    q4[gg] = reinterpret_cast<const float4 *>(a.q + (size_t)n * kHd + (h * G + GH * half + gg) * kHeadDim)[lane];
+                    acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                m_run = -INFINITY;
+                l_run = 0.f;
+            }
+            const int rows = min(kAttnRowsPerStage, r1 - t);
+            const float4 *ks = reinterpret_cast<const float4 *>(ring.stage(s));
+            const float4 *vs = reinterpret_cast<const float4 *>(ring.stage(s) + kAttnStageBytes / 2);
+            const int mine = min(4, rows - 4 * quad);
+            float4 k4[4], v4[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const bool in = i < mine;
+                k4[i] = in ? ks[(4 * quad + i) * (kHeadDim / 4) + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+                v4[i] = in ? vs[(4 * quad + i) * (kHeadDim / 4) + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ring.empty[s]);
+            g++;
+            if (mine > 0) flash_step3(q4, k4, v4, mine, lane, scale2, m_run, l_run, acc);
+            if (t + kAttnRowsPerStage < r1) continue;
+            // Last stage of the item: merge, per query head, the eight warps that
+            // hold it (same half), in warp order, into the chunk's partial.
+            attn_consumers_sync();
+#pragma unroll
+            for (int gg = 0; gg < GH; gg++) {
+                reinterpret_cast<float4 *>(wacc[warp][gg])[lane] = acc[gg];
+                const float mg = __shfl_sync(0xffffffffu, m_run, gg), lg = __shfl_sync(0xffffffffu, l_run, gg);
+                if (lane == 0) {
+                    wm[warp][gg] = mg;
+                    wl[warp][gg] = lg;
+                }
+            }
+            attn_consumers_sync();
+            float *hp = a.part + ((size_t)n * 2 + h) * kAttnItemMax * kAttnPartialFloats;
+            float *pc = hp + (size_t)c * kAttnPartialFloats;
+            for (int o = tid; o < G * kHeadDim; o += kBatchAttnWarps * 32) {
+                const int gq = o / kHeadDim, d = o % kHeadDim, hf = gq / GH, gg = gq % GH;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = hf; w < kBatchAttnWarps; w += 2) M = fmaxf(M, wm[w][gg]);
+                float num = 0.f, den = 0.f;
+#pragma unroll
+                for (int w = hf; w < kBatchAttnWarps; w += 2) {
+                    if (wm[w][gg] == -INFINITY) continue;
+                    const float e = exp2f(wm[w][gg] - M);
+                    den = fmaf(e, wl[w][gg], den);
+                    num = fmaf(e, wacc[w][gg][d], num);
+                }
+                pc[2 * kAttnMaxGroup + gq * kHeadDim + d] = num;
+                if (d == 0) {
+                    pc[gq] = M;
+                    pc[kAttnMaxGroup + gq] = den;
+                }
+            }
+            __threadfence();
+            attn_consumers_sync();
+            const int nchunks = (a.st->position[n] + a.item_rows) / a.item_rows;
+            unsigned *counter = &a.counters[n * 2 + h];
+            if (tid == 0) last_s = atomicAdd(counter, 1u) == (unsigned)(nchunks - 1);
+            attn_consumers_sync();
+            if (last_s) {
+                __threadfence();
+                for (int o = tid; o < G * kHeadDim; o += kBatchAttnWarps * 32) {
+                    const int gq = o / kHeadDim, d = o % kHeadDim;
+                    float M = -INFINITY;
+                    for (int cc = 0; cc < nchunks; cc++) M = fmaxf(M, __ldcg(hp + (size_t)cc * kAttnPartialFloats + gq));
+                    float num = 0.f, den = 0.f;
+                    for (int cc = 0; cc < nchunks; cc++) {
+                        const float *pp = hp + (size_t)cc * kAttnPartialFloats;
+                        const float mc = __ldcg(pp + gq);
+                        if (mc == -INFINITY) continue;
+                        const float e = exp2f(mc - M);
+                        den = fmaf(e, __ldcg(pp + kAttnMaxGroup + gq), den);
+                        num = fmaf(e, __ldcg(pp + 2 * kAttnMaxGroup + gq * kHeadDim + d), num);
+                    }
+                    uint16_t hi, lo;
+                    split_bf16(__fdiv_rn(num, den), hi, lo);
+                    a.oh[(size_t)n * kHd + (h * G + gq) * kHeadDim + d] = hi;
+                    a.ol[(size_t)n * kHd + (h * G + gq) * kHeadDim + d] = lo;
+                }
+                if (tid == 0) *counter = 0u;
+            }
+        }
+        if (tid == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 3] = global_ns();
+    }
+    // The last CTA out resets the work counter for the next launch.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&a.work[1], 1u) == gridDim.x - 1) {
+            a.work[0] = 0u;
+            a.work[1] = 0u;
+        }
+    }
 }
 
 // ---------------------------------------------------------------- top-2 per session
+// kTopBlocks blocks per session scan a slice of its logits each (float4 loads,
+// finite check) and publish a partial top-2; the last block of the session to
+// arrive merges the partials in order, logs the top-2 and feeds top-1 back as
+// the session's next token.
+constexpr int kTopBlocks = 16;
 struct Top2Args {
     BatchState *st;
-    const Top2 *part;  // [tiles][kBN]
-    int tiles;
-    TcmTop2 *log;      // [kBatchLogCap][kBN]
+    Top2 *part;          // [kBN][kTopBlocks]
+    unsigned *counters;  // [kBN]
+    int vocab;
+    TcmTop2 *log;        // [kBatchLogCap][kBN]
 };
 __global__ void __launch_bounds__(256) batch_top2_kernel(Top2Args a) {
     __shared__ Top2 sh[8];
+    __shared__ int last_s;
     pdl_trigger();
     pdl_wait();
-    const int n = blockIdx.x, tid = threadIdx.x;
+    const int n = blockIdx.y, tid = threadIdx.x;
     if (n >= a.st->n) return;
+    const int chunk = a.vocab / kTopBlocks, v0 = blockIdx.x * chunk;
+    const float4 *lg = reinterpret_cast<const float4 *>(a.st->logits[n] + v0);
     Top2 z = top2_empty();
-    for (int t = tid; t < a.tiles; t += 256) {
-        const Top2 p = a.part[(size_t)t * kBN + n];
-        top2_insert(z, p.a, p.ai);
-        top2_insert(z, p.b, p.bi);
+    bool bad = false;
+    for (int i = tid; i < chunk / 4; i += 256) {
+        const float4 v = __ldcg(lg + i);
+        bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+        const int id = v0 + 4 * i;
+        top2_insert(z, v.x, id);
+        top2_insert(z, v.y, id + 1);
+        top2_insert(z, v.z, id + 2);
+        top2_insert(z, v.w, id + 3);
     }
     top2_merge_warp(z);
+    if (__syncthreads_or(bad) && tid == 0) a.st->bad[n] = 1;
     if ((tid & 31) == 0) sh[tid >> 5] = z;
     __syncthreads();
     if (tid == 0) {
@@ -329,12 +615,25 @@ __global__ void __launch_bounds__(256) batch_top2_kernel(Top2Args a) {
             top2_insert(f, sh[w].a, sh[w].ai);
             top2_insert(f, sh[w].b, sh[w].bi);
         }
-        TcmTop2 top;
-        top.first = f.ai; top.second = f.bi; top.first_value = f.a; top.second_value = f.b;
-        a.log[(size_t)(a.st->step % kBatchLogCap) * kBN + n] = top;
-        a.st->token[n] = f.ai;
-        a.st->position[n] += 1;
+        a.part[(size_t)n * kTopBlocks + blockIdx.x] = f;
+        __threadfence();
+        last_s = atomicAdd(&a.counters[n], 1u) == kTopBlocks - 1;
     }
+    __syncthreads();
+    if (!last_s || tid != 0) return;
+    __threadfence();
+    Top2 f = top2_empty();
+    for (int b = 0; b < kTopBlocks; b++) {
+        const Top2 p = a.part[(size_t)n * kTopBlocks + b];
+        top2_insert(f, p.a, p.ai);
+        top2_insert(f, p.b, p.bi);
+    }
+    TcmTop2 top;
+    top.first = f.ai; top.second = f.bi; top.first_value = f.a; top.second_value = f.b;
+    a.log[(size_t)(a.st->step % kBatchLogCap) * kBN + n] = top;
+    a.st->token[n] = f.ai;
+    a.st->position[n] += 1;
+    a.counters[n] = 0u;
 }
 __global__ void batch_step_end_kernel(BatchState *st) {
     pdl_wait();
@@ -375,6 +674,7 @@ CUtensorMap bf16_map(const void *base, uint64_t inner, uint64_t rows, uint32_t b
 template <class Epi> void gemm_setup() {
     TCM_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<kBN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)TcGeo<kBN>::kSmem));
+    TCM_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<kBN, Epi>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
 }
 
 }  // namespace
@@ -400,9 +700,12 @@ struct QwenB200Batch {
     BatchState *host;     // pinned mirror
     float *x, *q, *part, *attn_part;
     uint16_t *nh, *nl, *hh, *hl;
-    unsigned *counters, *attn_counters;
+    unsigned *counters, *attn_counters, *top_counters, *attn_work;
     Top2 *top_part;
+    int cluster_qkv, cluster_o, cluster_down;  // split clusters (0: split K through global memory)
+    int attn_item_rows;   // cache rows per attention work item
     TcmTop2 *log, *host_log;
+    unsigned long long *trace;  // stage timeline (measurement only), or null
     int readout_tiles;
     std::map<int, cudaGraphExec_t> graphs;
     int launches;
@@ -413,7 +716,7 @@ namespace {
 template <class Epi>
 void launch_gemm(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1, const CUtensorMap &a2,
                  const CUtensorMap &xh, const CUtensorMap &xl, int tiles, int splits, int kblocks, const Epi &epi,
-                 bool pdl) {
+                 bool pdl, int cluster = 1) {
     TcArgs<kBN, Epi> args;
     args.a[0] = a0;
     args.a[1] = a1;
@@ -423,13 +726,72 @@ void launch_gemm(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1,
     args.tiles = tiles;
     args.splits = splits;
     args.kblocks = kblocks;
+    args.cluster = cluster;
     args.part = b->part;
     args.counters = b->counters;
     args.err = &b->st->err;
-    args.trace = nullptr;
+    args.trace = b->trace;
     args.epi = epi;
-    const int items = tiles * splits, grid = items < sm_count() ? items : sm_count();
+    const int items = tiles * splits;
+    if (cluster > 1) {
+        // One item per CTA; a cluster of `splits` CTAs per tile.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(items);
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = TcGeo<kBN>::kSmem;
+        cfg.stream = stream();
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 2 : 1;
+        TCM_CUDA(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kBN, Epi>, args));
+        return;
+    }
+    const int grid = items < sm_count() ? items : sm_count();
     launch(tc_gemm_kernel<kBN, Epi>, dim3(grid), dim3(kTcThreads), TcGeo<kBN>::kSmem, stream(), pdl, args);
+}
+
+// A K-split GEMM of `tiles` 128-row tiles: split across a cluster when one
+// fits (cluster > 0), else 12 splits meeting in global memory.
+template <class Epi>
+void launch_split(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1, const CUtensorMap &a2,
+                  const CUtensorMap &xh, const CUtensorMap &xl, int tiles, int kblocks, const Epi &epi, bool pdl,
+                  int cluster) {
+    if (cluster > 0) launch_gemm(b, a0, a1, a2, xh, xl, tiles, cluster, kblocks, epi, pdl, cluster);
+    else launch_gemm(b, a0, a1, a2, xh, xl, tiles, kblocks < 12 ? kblocks : 12, kblocks, epi, pdl, 1);
+}
+
+// How many clusters of `size` GEMM CTAs the GPU can hold at once.
+int cluster_capacity(int size) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size * 16);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = TcGeo<kBN>::kSmem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = size;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_kernel<kBN, EpiResid>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        clusters = 0;
+    }
+    return clusters;
+}
+// The largest split cluster (4 <= S <= 16, the fold's slice bound) whose
+// `tiles` clusters all fit on the GPU at once; 0 when none does.
+int pick_cluster(int tiles, int kblocks) {
+    for (int sz = 16; sz >= 4; sz--)
+        if (sz <= kblocks && cluster_capacity(sz) >= tiles) return sz;
+    return 0;
 }
 
 void launch_rms(QwenB200Batch *b, const float *w, bool embed, bool copy_x, bool pdl) {
@@ -445,23 +807,24 @@ void launch_step(QwenB200Batch *b, int n) {
     for (int l = 0; l < s.layers; l++) {
         const LayerMaps &m = b->maps[l];
         EpiQkv qkv = {b->st, L[l].qb, L[l].kb, L[l].vb, b->rope_den, b->q, l};
-        launch_gemm(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, 9, kHd / kTcKBlock, qkv, true);
-        AttnArgs at = {b->st, b->q, l, 1.0f / sqrtf((float)kHeadDim), b->attn_part, b->attn_counters, b->nh, b->nl};
-        launch(batch_attn_kernel, dim3(kAttnSplitMax, 2, n), dim3(kDecodeAttnThreads), 0, stream(), true, at);
+        launch_split(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, kHd / kTcKBlock, qkv, true, b->cluster_qkv);
+        AttnArgs at = {b->st, b->q, l, 1.0f / sqrtf((float)kHeadDim), b->attn_part, b->attn_counters, b->nh, b->nl,
+                       nullptr, b->attn_work + 2 * l, b->attn_item_rows};
+        launch(batch_attn_kernel, dim3(sm_count()), dim3(kBatchAttnThreads), kAttnSmem, stream(), true, at);
         EpiResid o = {b->st, b->x};
-        launch_gemm(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, 12, kHd / kTcKBlock, o, true);
+        launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, true, b->cluster_o);
         launch_rms(b, L[l].post_norm, false, false, true);
         EpiSwiglu sw = {b->st, b->hh, b->hl};
         launch_gemm(b, m.gate, m.up, m.up, b->nh_map, b->nl_map, kFf / 64, 1, kHd / kTcKBlock, sw, true);
         EpiResid dn = {b->st, b->x};
-        launch_gemm(b, m.down, m.down, m.down, b->hh_map, b->hl_map, 12, 12, kFf / kTcKBlock, dn, true);
+        launch_split(b, m.down, m.down, m.down, b->hh_map, b->hl_map, 12, kFf / kTcKBlock, dn, true, b->cluster_down);
         if (l + 1 < s.layers) launch_rms(b, L[l + 1].input_norm, false, false, true);
     }
     launch_rms(b, b->final_norm, false, true, true);
-    EpiLogits lg = {b->st, b->top_part};
+    EpiLogits lg = {b->st};
     launch_gemm(b, b->embed, b->embed, b->embed, b->nh_map, b->nl_map, b->readout_tiles, 1, kHd / kTcKBlock, lg, true);
-    Top2Args ta = {b->st, b->top_part, b->readout_tiles, b->log};
-    launch(batch_top2_kernel, dim3(n), dim3(256), 0, stream(), true, ta);
+    Top2Args ta = {b->st, b->top_part, b->top_counters, b->s.vocab, b->log};
+    launch(batch_top2_kernel, dim3(kTopBlocks, n), dim3(256), 0, stream(), true, ta);
     launch(batch_step_end_kernel, dim3(1), dim3(1), 0, stream(), true, b->st);
 }
 
@@ -505,19 +868,22 @@ bool load_sessions(QwenB200Batch *b, int n, const QwenB200BatchSession *ss, cons
     return true;
 }
 
-int read_back(QwenB200Batch *b, int n, int steps, TcmTop2 *tops) {
+int read_back(QwenB200Batch *b, int n, int steps, TcmTop2 *tops, bool history = false) {
     TCM_CUDA(cudaMemcpyAsync(b->host, b->st, sizeof(BatchState), cudaMemcpyDeviceToHost, stream()));
-    TCM_CUDA(cudaMemcpyAsync(b->host_log, b->log, sizeof(TcmTop2) * kBatchLogCap * kBN, cudaMemcpyDeviceToHost,
-                             stream()));
+    const int last = (steps - 1) % kBatchLogCap;
+    if (history)
+        TCM_CUDA(cudaMemcpyAsync(b->host_log, b->log, sizeof(TcmTop2) * kBatchLogCap * kBN, cudaMemcpyDeviceToHost,
+                                 stream()));
+    else
+        TCM_CUDA(cudaMemcpyAsync(b->host_log + (size_t)last * kBN, b->log + (size_t)last * kBN,
+                                 sizeof(TcmTop2) * kBN, cudaMemcpyDeviceToHost, stream()));
     TCM_CUDA(cudaStreamSynchronize(stream()));
     if (b->host->err) {
         fprintf(stderr, "B200 batch decode: a pipeline wait ran out (bits 0x%x)\n", b->host->err);
         return -4;
     }
-    if (tops) {
-        const int last = (steps - 1) % kBatchLogCap;
+    if (tops)
         for (int i = 0; i < n; i++) tops[i] = b->host_log[(size_t)last * kBN + i];
-    }
     for (int i = 0; i < n; i++)
         if (b->host->bad[i]) return -3;
     return 0;
@@ -543,6 +909,7 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
         gemm_setup<EpiSwiglu>();
         gemm_setup<EpiLogits>();
         gemm_setup<EpiStore>();
+        TCM_CUDA(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem));
     });
     QwenB200Batch *b = new QwenB200Batch();
     b->d = d;
@@ -587,10 +954,20 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
     b->part = (float *)gpu_alloc((size_t)16 * 12 * 128 * kBN * 4);
     b->counters = (unsigned *)gpu_alloc(256 * 4);
     gpu_zero(b->counters, 256 * 4);
-    b->attn_part = (float *)gpu_alloc((size_t)kBN * 2 * kAttnSplitMax * kAttnPartialFloats * 4);
+    b->attn_part = (float *)gpu_alloc((size_t)kBN * 2 * kAttnItemMax * kAttnPartialFloats * 4);
     b->attn_counters = (unsigned *)gpu_alloc((size_t)kBN * 2 * 4);
     gpu_zero(b->attn_counters, (size_t)kBN * 2 * 4);
-    b->top_part = (Top2 *)gpu_alloc((size_t)b->readout_tiles * kBN * sizeof(Top2));
+    b->top_part = (Top2 *)gpu_alloc((size_t)kBN * kTopBlocks * sizeof(Top2));
+    b->top_counters = (unsigned *)gpu_alloc(kBN * 4);
+    gpu_zero(b->top_counters, kBN * 4);
+    // One work counter pair per layer: a launch touches its counters before its
+    // dependency wait, so neighbouring layers must not share them.
+    b->attn_work = (unsigned *)gpu_alloc((size_t)s.layers * 2 * 4);
+    gpu_zero(b->attn_work, (size_t)s.layers * 2 * 4);
+    b->attn_item_rows = 1024;
+    b->cluster_qkv = pick_cluster(16, kHd / kTcKBlock);
+    b->cluster_o = pick_cluster(12, kHd / kTcKBlock);
+    b->cluster_down = pick_cluster(12, kFf / kTcKBlock);
     b->log = (TcmTop2 *)gpu_alloc(sizeof(TcmTop2) * kBatchLogCap * kBN);
     TCM_CUDA(cudaMallocHost((void **)&b->host_log, sizeof(TcmTop2) * kBatchLogCap * kBN));
     b->launches = 1 + s.layers * 7 + 3;
@@ -602,7 +979,7 @@ void qwen_b200_batch_free(QwenB200Batch *b) {
     TCM_CUDA(cudaStreamSynchronize(stream()));
     for (auto &g : b->graphs) TCM_CUDA(cudaGraphExecDestroy(g.second));
     void *all[] = {b->st, b->x, b->q, b->nh, b->nl, b->hh, b->hl, b->part, b->counters, b->attn_part,
-                   b->attn_counters, b->top_part, b->log};
+                   b->attn_counters, b->top_part, b->log, b->top_counters, b->attn_work};
     for (void *p : all) gpu_free(p);
     TCM_CUDA(cudaFreeHost(b->host));
     TCM_CUDA(cudaFreeHost(b->host_log));
@@ -611,6 +988,104 @@ void qwen_b200_batch_free(QwenB200Batch *b) {
 }
 
 int qwen_b200_batch_max(void) { return kBN; }
+
+int qwen_b200_batch_tune(QwenB200Batch *b, int key, int value) {
+    if (!b) return -1;
+    if (key == 0) {  // attention rows per work item
+        if (value < kAttnItemRowsMin || value > 2048 || value % kAttnRowsPerStage) return -1;
+        TCM_CUDA(cudaStreamSynchronize(stream()));
+        for (auto &g : b->graphs) TCM_CUDA(cudaGraphExecDestroy(g.second));
+        b->graphs.clear();
+        b->attn_item_rows = value;
+        return 0;
+    }
+    return -1;
+}
+
+int qwen_b200_batch_cluster_capacity(int size) { return size >= 1 && size <= 16 ? cluster_capacity(size) : -1; }
+int qwen_b200_batch_clusters(const QwenB200Batch *b, int *qkv, int *o, int *down) {
+    if (!b) return -1;
+    *qkv = b->cluster_qkv;
+    *o = b->cluster_o;
+    *down = b->cluster_down;
+    return 0;
+}
+
+float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                                 const int *positions, int stage, int layer, int reps);
+
+int qwen_b200_batch_trace_stage(QwenB200Batch *b, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                                const int *positions, int stage, int layer, unsigned long long *host, int ctas) {
+    if (!b || !host || ctas < 1 || ctas > 1024) return -1;
+    const size_t bytes = (size_t)1024 * 8 * sizeof(unsigned long long);
+    b->trace = (unsigned long long *)gpu_alloc(bytes);
+    gpu_zero(b->trace, bytes);
+    const float ms = qwen_b200_batch_time_stage(b, n, sessions, tokens, positions, stage, layer, 1);
+    gpu_read(host, b->trace, (size_t)ctas * 8 * sizeof(unsigned long long));
+    gpu_free(b->trace);
+    b->trace = nullptr;
+    return ms < 0.f ? -1 : 0;
+}
+
+float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                                 const int *positions, int stage, int layer, int reps) {
+    if (!b || stage < 0 || stage > 6 || layer < 0 || layer >= b->s.layers || reps < 1 ||
+        !load_sessions(b, n, sessions, tokens, positions))
+        return -1.f;
+    const std::vector<QwenB200Layer> &L = *b->layers;
+    const LayerMaps &m = b->maps[layer];
+    auto once = [&]() {
+        switch (stage) {
+            case 0: {
+                EpiQkv qkv = {b->st, L[layer].qb, L[layer].kb, L[layer].vb, b->rope_den, b->q, layer};
+                launch_split(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, kHd / kTcKBlock, qkv, false, b->cluster_qkv);
+                break;
+            }
+            case 1: {
+                AttnArgs at = {b->st, b->q, layer, 1.0f / sqrtf((float)kHeadDim), b->attn_part, b->attn_counters,
+                               b->nh, b->nl, b->trace, b->attn_work + 2 * layer, b->attn_item_rows};
+                launch(batch_attn_kernel, dim3(sm_count()), dim3(kBatchAttnThreads), kAttnSmem, stream(), false, at);
+                break;
+            }
+            case 2: {
+                EpiResid o = {b->st, b->x};
+                launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, false, b->cluster_o);
+                break;
+            }
+            case 3: {
+                EpiSwiglu sw = {b->st, b->hh, b->hl};
+                launch_gemm(b, m.gate, m.up, m.up, b->nh_map, b->nl_map, kFf / 64, 1, kHd / kTcKBlock, sw, false);
+                break;
+            }
+            case 4: {
+                EpiResid dn = {b->st, b->x};
+                launch_split(b, m.down, m.down, m.down, b->hh_map, b->hl_map, 12, kFf / kTcKBlock, dn, false,
+                             b->cluster_down);
+                break;
+            }
+            case 5: {
+                EpiLogits lg = {b->st};
+                launch_gemm(b, b->embed, b->embed, b->embed, b->nh_map, b->nl_map, b->readout_tiles, 1,
+                            kHd / kTcKBlock, lg, false);
+                break;
+            }
+            default: launch_rms(b, L[layer].post_norm, false, false, false); break;
+        }
+    };
+    once();
+    cudaEvent_t e0, e1;
+    TCM_CUDA(cudaEventCreate(&e0));
+    TCM_CUDA(cudaEventCreate(&e1));
+    TCM_CUDA(cudaEventRecord(e0, stream()));
+    for (int i = 0; i < reps; i++) once();
+    TCM_CUDA(cudaEventRecord(e1, stream()));
+    TCM_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    TCM_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    TCM_CUDA(cudaEventDestroy(e0));
+    TCM_CUDA(cudaEventDestroy(e1));
+    return ms / reps;
+}
 
 int qwen_b200_batch_matmul(const void *w, int rows, int in, const float *x, int n, float *y, int splits) {
     if (!w || !x || !y || rows < 128 || rows % 128 || in < 64 || in % 64 || n < 1 || n > kBN || splits < 1 ||
@@ -635,6 +1110,7 @@ int qwen_b200_batch_matmul(const void *w, int rows, int in, const float *x, int 
     a.tiles = tiles;
     a.splits = splits;
     a.kblocks = in / 64;
+    a.cluster = 1;
     a.part = part;
     a.counters = counters;
     a.err = err;
@@ -672,7 +1148,7 @@ int qwen_b200_batch_enqueue(QwenB200Batch *b, int n, const QwenB200BatchSession 
 
 int qwen_b200_batch_read(QwenB200Batch *b, int n, int steps, TcmTop2 *tops, TcmTop2 *history) {
     if (!b || n < 1 || n > kBN || steps < 1 || steps > kBatchLogCap) return -1;
-    const int status = read_back(b, n, steps, tops);
+    const int status = read_back(b, n, steps, tops, history != nullptr);
     if (history)
         for (int t = 0; t < steps; t++)
             for (int i = 0; i < n; i++) history[(size_t)t * n + i] = b->host_log[(size_t)t * kBN + i];

@@ -22,13 +22,21 @@
 //           32 * (w % 4) ...), then either the tile's final values or, with
 //           split K, a partial to global memory of which the last CTA to arrive
 //           sums the splits in order (deterministic) and finishes the tile.
+// With split K launched as thread-block clusters (one cluster of `splits` CTAs
+// per tile, one item per CTA), every CTA leaves its partial tile in shared
+// memory, and after a cluster barrier each rank folds its own slice of row
+// pairs from all ranks through distributed shared memory, in rank order
+// (deterministic), and writes that slice's outputs; a second barrier keeps the
+// partials alive until every rank has read them.
 // The tile goes to shared memory as [128][N + 1] FP32 and the epilogue functor
-// writes the outputs (bias, RoPE, K/V append, residual, SwiGLU, logits ...).
+// writes the outputs for row pairs (p, p + 64) (bias, RoPE, K/V append,
+// residual, SwiGLU, logits ...).
 // Every wait is bounded by the global timer and sets a bit in *err.
 #pragma once
 #include "common.cuh"
 #include "stream.cuh"
 #include <cuda.h>
+#include <cooperative_groups.h>
 
 namespace tcm {
 
@@ -46,7 +54,8 @@ template <int N> struct TcGeo {
     static constexpr int kNP = N + 1;                           // padded tile row (floats)
     static constexpr uint32_t kTileBytes = 128 * kNP * 4;
     static constexpr uint32_t kTmemCols = 2 * N < 32 ? 32 : 2 * N;
-    static constexpr size_t kSmem = 1024 + (size_t)kStages * kStage + kTileBytes + 256;
+    static constexpr uint32_t kScratch = 2048;                  // epilogue metadata (per-session pointers)
+    static constexpr size_t kSmem = 1024 + (size_t)kStages * kStage + kTileBytes + kScratch + 256;
     // Instruction descriptor: F32 accumulate, BF16 A and B, both K-major, M = 128.
     static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (8u << 24);
 };
@@ -98,10 +107,20 @@ struct TcRows {
     int m0, r0, m1, r1;
 };
 
+// Optional timeline: per CTA, global-timer stamps (ns) at
+//   0 entry after setup, 1 producer released by the dependency wait,
+//   2 first stage ready (MMA), 3 last MMA committed, 4 epilogue released,
+//   5 first accumulator read, 6 last tile stored, 7 exit.
+constexpr int kTcMarks = 8;
+__device__ __forceinline__ void tc_mark(unsigned long long *trace, int k) {
+    if (trace) trace[(size_t)blockIdx.x * kTcMarks + k] = global_ns();
+}
+
 template <int N, class Epi> struct TcArgs {
     CUtensorMap a[3];
     CUtensorMap xh, xl;
     int tiles, splits, kblocks;
+    int cluster;          // 1: splits meet in global memory; = splits: in a thread-block cluster
     float *part;          // split-K partials [tile][split][128][N]
     unsigned *counters;   // per tile, reset by the finishing CTA
     unsigned *err;
@@ -115,7 +134,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float(*tile)[G::kNP] = reinterpret_cast<float(*)[G::kNP]>(smem + (size_t)G::kStages * G::kStage);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)G::kStages * G::kStage + G::kTileBytes);
+    unsigned char *scratch = smem + (size_t)G::kStages * G::kStage + G::kTileBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(scratch + G::kScratch);
     uint64_t *full = bars, *empty = bars + G::kStages, *acc_full = bars + 2 * G::kStages,
              *acc_free = acc_full + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_free + 2);
@@ -144,6 +164,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     pdl_trigger();
+    if (threadIdx.x == 0) tc_mark(a.trace, 0);
 
     auto krange = [&](int item, int &t, int &k0, int &k1) {
         t = item / a.splits;
@@ -170,6 +191,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 }
             };
             if (item < items) open_item();
+            for (int i = 0; i < 3; i++) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.a[i])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.xh)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.xl)) : "memory");
             auto load_w = [&](int s) {
                 unsigned char *st = smem + (size_t)s * G::kStage;
                 mbar_expect_tx(&full[s], G::kStage);
@@ -190,6 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 step();
             }
             pdl_wait();
+            tc_mark(a.trace, 1);
             for (int j = 0; j < g; j++) load_x(j, pro_kb[j]);
             for (; item < items; g++) {
                 const int s = g % G::kStages;
@@ -221,6 +246,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         break;
                     }
                     tc_fence_after();
+                    if (g == 0) tc_mark(a.trace, 2);
                     const uint32_t base = smem_addr(smem + (size_t)s * G::kStage);
                     const uint64_t ad = tc_desc(base), hd = tc_desc(base + kTcATile),
                                    ld = tc_desc(base + kTcATile + G::kBTile);
@@ -235,11 +261,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 if (!ok) break;
                 tc_commit(&acc_full[buf]);
             }
+            tc_mark(a.trace, 3);
         }
     } else {
         // Epilogue: 128 threads, thread e owns tile row e (tensor-memory lane).
         const int e = (warp & 3) * 32 + lane;  // warps 2..5 -> lane quarters 2,3,0,1
         pdl_wait();
+        if (e == 0) tc_mark(a.trace, 4);
+        a.epi.init(scratch, e);
+        epi_sync();
         int local = 0;
         for (int item = blockIdx.x; item < items; item += gridDim.x, local++) {
             int t, k0, k1;
@@ -247,6 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const int buf = local & 1;
             if (!mbar_wait(&acc_full[buf], (local >> 1) & 1, a.err, kTcErrAcc)) break;
             tc_fence_after();
+            if (e == 0 && local == 0) tc_mark(a.trace, 5);
             float v[N];
             const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * N);
 #pragma unroll
@@ -258,6 +289,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
             tc_fence_before();
             mbar_arrive(&acc_free[buf]);
+            if (a.cluster > 1) {
+                // Partial to this CTA's shared tile; the cluster folds it below.
+                epi_sync();
+#pragma unroll
+                for (int c = 0; c < N; c++) tile[e][c] = v[c];
+                continue;
+            }
             bool finish = true;
             if (a.splits > 1) {
                 const int split = item % a.splits;
@@ -292,12 +330,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
                 for (int c = 0; c < N; c++) tile[e][c] = v[c];
                 epi_sync();
-                a.epi.store(t, tile, e);
+                a.epi.store(t, tile, 0, 64, e, scratch);
             }
+        }
+        if (e == 0) tc_mark(a.trace, 6);
+    }
+    if (a.cluster > 1) {
+        // Cluster fold: rank r owns row pairs [r * 64 / S, (r + 1) * 64 / S).
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (warp >= 2) {
+            const int S = a.cluster, r = (int)cluster.block_rank(), t = blockIdx.x / S;
+            const int p0 = r * 64 / S, p1 = (r + 1) * 64 / S, count = (p1 - p0) * 2 * N;
+            const int e = (warp & 3) * 32 + lane;
+            // Sums of the slice in registers: S >= 4 gives at most 16 pairs, 2 rows
+            // each, N columns, over 128 threads.
+            constexpr int kMaxPer = (16 * 2 * N + 127) / 128;
+            float sum[kMaxPer];
+#pragma unroll
+            for (int j = 0; j < kMaxPer; j++) {
+                const int idx = e + 128 * j;
+                sum[j] = 0.f;
+                if (idx < count) {
+                    const int pr = idx / (2 * N), rem = idx % (2 * N), half = rem / N, c = rem % N;
+                    const int row = p0 + pr + 64 * half;
+                    for (int q = 0; q < S; q++) sum[j] += cluster.map_shared_rank(&tile[row][c], q)[0];
+                }
+            }
+            cluster.sync();  // every rank has read every partial it needs
+#pragma unroll
+            for (int j = 0; j < kMaxPer; j++) {
+                const int idx = e + 128 * j;
+                if (idx < count) {
+                    const int pr = idx / (2 * N), rem = idx % (2 * N), half = rem / N, c = rem % N;
+                    tile[p0 + pr + 64 * half][c] = sum[j];
+                }
+            }
+            epi_sync();
+            a.epi.store(t, tile, p0, p1, e, scratch);
+            if (e == 0) tc_mark(a.trace, 6);
+        } else {
+            cluster.sync();
         }
     }
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) tc_mark(a.trace, 7);
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::kTmemCols));

@@ -397,7 +397,7 @@ int qwen_push_batch(QwenSession **ss, int n, const int *tokens) {
     if (!m->fused || m->matrix_dtype != 2) return -1;
     for (int i = 0; i < n; i++) {
         QwenSession *s = ss[i];
-        if (s->model != m || !fused_token_ok(s) || begin_guards(s, tokens[i]) || s->position >= 8192) return -1;
+        if (s->model != m || !fused_token_ok(s) || begin_guards(s, tokens[i]) || s->position >= 9216) return -1;
         for (int j = 0; j < i; j++)
             if (ss[j] == s) return -1;
     }

@@ -31,6 +31,20 @@ void qwen_b200_session_view(const QwenSession *s, QwenSessionView *v) {
 
 void qwen_b200_session_set_delivered(QwenSession *s, int delivered) { s->delivered = delivered; }
 
+/* Benchmark aid: place a session's cursor after a context of `position` rows
+ * whose K/V were written into the session's cache by other means (a seeded
+ * fill), with `pending` as the next token. Only at a token boundary with no
+ * stack frames; returns 0 or -1. */
+int qwen_b200_session_set_cursor(QwenSession *s, int position, int pending) {
+    if (s->phase == 2 || s->depth || position < 1 || position > s->capacity || pending < 0 ||
+        pending >= s->model->vocab)
+        return -1;
+    s->position = position;
+    s->pending = pending;
+    s->phase = 1;
+    return 0;
+}
+
 void qwen_b200_session_observe(QwenSession *s, QwenObserver observer, void *context, int position, int layer) {
     s->observer = observer;
     s->observer_context = context;

@@ -153,7 +153,7 @@ int qwen_complete_token(QwenSession *);
  * separate qwen_push calls would leave them. All sessions must be distinct,
  * belong to a BF16 model with the fused decoder, keep their K/V in the session
  * (no cache callbacks), have no port observed at their position, and pass
- * qwen_push's guards; n <= 64, positions < 8192. Returns 0, or -1 with nothing
+ * qwen_push's guards; n <= 64, positions < 9216. Returns 0, or -1 with nothing
  * changed. */
 int qwen_push_batch(QwenSession **sessions, int n, const int *tokens);
 

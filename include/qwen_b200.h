@@ -159,7 +159,7 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *);
 void qwen_b200_batch_free(QwenB200Batch *);
 int qwen_b200_batch_max(void);
 int qwen_b200_batch_launches_per_step(const QwenB200Batch *);
-/* One step: session i takes tokens[i] at positions[i] (position < 8192); tops[i]
+/* One step: session i takes tokens[i] at positions[i] (position < 9216); tops[i]
  * receives its top-2. 0, -1 invalid arguments (nothing ran), -3 non-finite
  * logits, -4 a pipeline wait ran out. */
 int qwen_b200_batch_step(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
@@ -174,6 +174,25 @@ int qwen_b200_batch_read(QwenB200Batch *, int n, int steps, TcmTop2 *tops, TcmTo
  * (rows a multiple of 128, in a multiple of 64) and n <= 64 FP32 rows x, with
  * `splits` K-splits. Synchronous; 0, -1 invalid, -4 wait ran out. */
 int qwen_b200_batch_matmul(const void *w, int rows, int in, const float *x, int n, float *y, int splits);
+/* Measurement aid: mean device time (ms) of one standalone launch of a step's
+ * stage for these sessions: 0 q/k/v GEMM (appends this step's K/V rows), 1
+ * attention, 2 O GEMM, 3 gate/up GEMM, 4 down GEMM, 5 vocabulary GEMM, 6
+ * RMSNorm, of `layer`, over `reps` launches. */
+float qwen_b200_batch_time_stage(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                                 const int *positions, int stage, int layer, int reps);
+/* The same launch with a per-CTA timeline: host receives ctas x 8 global-timer
+ * stamps (ns; GEMM: entry, producer released, first stage ready, last MMA
+ * committed, epilogue released, first accumulator read, last tile stored,
+ * exit; attention: entry, consumers released, first stage ready, done). */
+int qwen_b200_batch_trace_stage(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
+                                const int *positions, int stage, int layer, unsigned long long *host, int ctas);
+/* How many thread-block clusters of `size` GEMM CTAs the GPU holds at once, and
+ * the split-K cluster sizes the engine chose (0: split through global memory). */
+int qwen_b200_batch_cluster_capacity(int size);
+/* Tuning: key 0 = cache rows per attention work item (a multiple of 32 in
+ * [256, 2048], default 1024). Returns 0, or -1 for an unknown key or value. */
+int qwen_b200_batch_tune(QwenB200Batch *, int key, int value);
+int qwen_b200_batch_clusters(const QwenB200Batch *, int *qkv, int *o, int *down);
 
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
