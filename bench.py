@@ -450,6 +450,11 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
     pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     tc_peak = float(pk.get("bf16_tflops", 1590.0))
     gateup_bytes = 2 * shape.intermediate * shape.hidden * 2
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():  # ncu DRAM bytes per cache row (a 4,096-row capture), scaled to these rows
+        per_row = json.loads(tf.read_text()).get("batch_attn_bytes_per_row")
+        traffic = int(per_row * sum(p + 1 for p in pos)) if per_row else None
     L.qwen_b200_batch_free(batch)
     for s in sessions:
         s.free()

@@ -201,3 +201,14 @@ def test_cache_callback_layers(L):
     assert rewinds[-1] == (0, s.view().epoch)
     s.free()
     m.free()
+
+
+def test_push_batch_refuses_without_the_batched_engine(model):
+    """qwen_push_batch needs a BF16 model with the fused decoder; anything else is
+    refused with nothing changed (the CPU build has no fused decoder)."""
+    a, b = cm.Session(model, 32), cm.Session(model, 32)
+    prefix(a)
+    before = bytes(a._buf)
+    assert cm.push_batch([a, b], [1, 2]) == -1
+    assert cm.push_batch([a, a], [1, 2]) == -1
+    assert bytes(a._buf) == before
