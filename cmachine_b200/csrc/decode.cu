@@ -143,6 +143,8 @@ template <typename WT> __device__ __forceinline__ float row_dot(const unsigned c
     for (int k = 0; k < kNV<WT>; k++) acc = dot_vec(v[lane + 32 * k], &xr[Geo<WT>::E * k], acc, WT());
     return warp_sum(acc);
 }
+
+
 __device__ __forceinline__ int share_begin(int total, int part, int parts) { return (int)((long long)part * total / parts); }
 
 // Optional timeline trace: thread 0 of each CTA stamps the global timer at
@@ -321,6 +323,7 @@ struct GateUpArgs {
     float *h;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
+    unsigned *sched;            // row-group counter of this launch site
     float eps;
 };
 // Items alternate gate row j, up row j; the epilogue forms h_j = silu(g) * u
@@ -331,10 +334,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     constexpr int R = Geo<WT>::R;
     __shared__ float res[2][R];
     __shared__ __align__(16) float nw_s[kHidden];
-    __shared__ int fail_s;
+    __shared__ int fail_s, hdr_s[kStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j0 = share_begin(kInter, blockIdx.x, gridDim.x), j1 = share_begin(kInter, blockIdx.x + 1, gridDim.x);
-    const int items = 2 * (j1 - j0);
+    const int items = 2 * kInter;
     const WT *wg = (const WT *)a.wg, *wu = (const WT *)a.wu;
     if (threadIdx.x == 0) fail_s = 0;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
@@ -342,9 +344,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
-            ring_produce(ring, items, R, kRow<WT>,
-                         [&](int i) { return (const void *)((i & 1 ? wu : wg) + (size_t)(j0 + (i >> 1)) * kHidden); },
-                         &a.st->fault);
+            ring_produce_dynamic(ring, items, R, kRow<WT>,
+                                 [&](int i) { return (const void *)((i & 1 ? wu : wg) + (size_t)(i >> 1) * kHidden); },
+                                 a.sched, hdr_s, &a.st->fault);
         return;
     }
     stage_norm(nw_s, a.norm);
@@ -355,10 +357,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     consumers_sync();
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     trace_mark(a.trace, 2);
-    const int groups = (items + R - 1) / R;
-    for (int g = 0; g < groups; g++) {
-        const int n = min(R, items - g * R);
-        if (ring_acquire(ring, g, &a.st->fault)) {
+    for (int g = 0;; g++) {
+        bool failed = false;
+        const int grp = ring_next(ring, g, hdr_s, &a.st->fault, &failed);
+        const int n = grp >= 0 ? min(R, items - grp * R) : 0;
+        if (failed) fail_s = 1;
+        if (grp >= 0) {
             const unsigned char *stage = ring.stage(g % kStages);
 #pragma unroll
             for (int m = 0; m < R / kConsumerWarps; m++) {
@@ -368,16 +372,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
                     if (lane == 0) res[g & 1][j] = y;
                 }
             }
-        } else {
-            fail_s = 1;
+            ring_release(ring, g);
         }
-        ring_release(ring, g);
         consumers_sync();
-        if (fail_s) break;
+        if (fail_s || grp < 0) break;
         if ((int)threadIdx.x < n / 2) {
             const int t = threadIdx.x;
             const float gv = res[g & 1][2 * t], uv = res[g & 1][2 * t + 1];
-            a.h[j0 + (g * R) / 2 + t] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv);
+            a.h[(grp * R) / 2 + t] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv);
         }
     }
     trace_mark(a.trace, 3);
@@ -474,6 +476,7 @@ struct ReadoutArgs {
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
     TcmTop2 *log;
+    unsigned *sched;            // row-group counter of this launch site
     int vocab;
     float eps;
 };
@@ -484,18 +487,17 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     __shared__ float sv[2 * kConsumerWarps];
     __shared__ int si[2 * kConsumerWarps];
     __shared__ __align__(16) float nw_s[kHidden];
-    __shared__ int last;
+    __shared__ int last, hdr_s[kStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r0 = share_begin(a.vocab, blockIdx.x, gridDim.x), r1 = share_begin(a.vocab, blockIdx.x + 1, gridDim.x);
-    const int items = r1 - r0;
+    const int items = a.vocab;
     const WT *e = (const WT *)a.embed;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
-            ring_produce(ring, items, R, kRow<WT>, [&](int i) { return (const void *)(e + (size_t)(r0 + i) * kHidden); },
-                         &a.st->fault);
+            ring_produce_dynamic(ring, items, R, kRow<WT>, [&](int i) { return (const void *)(e + (size_t)i * kHidden); },
+                                 a.sched, hdr_s, &a.st->fault);
         return;
     }
     stage_norm(nw_s, a.norm);
@@ -508,16 +510,17 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     Top2 t = top2_empty();
     bool bad = false;
     trace_mark(a.trace, 2);
-    const int groups = (items + R - 1) / R;
-    for (int g = 0; g < groups; g++) {
-        if (!ring_acquire(ring, g, &a.st->fault)) break;
-        const int n = min(R, items - g * R);
+    for (int g = 0;; g++) {
+        bool failed = false;
+        const int grp = ring_next(ring, g, hdr_s, &a.st->fault, &failed);
+        if (grp < 0) break;
+        const int n = min(R, items - grp * R);
         const unsigned char *stage = ring.stage(g % kStages);
 #pragma unroll
         for (int m = 0; m < R / kConsumerWarps; m++) {
             const int j = warp + kConsumerWarps * m;
             if (j < n) {
-                const int row = r0 + g * R + j;
+                const int row = grp * R + j;
                 const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
                 if (lane == 0) a.logits[row] = y;
                 bad |= !isfinite(y);
@@ -684,12 +687,13 @@ struct QwenB200Runner {
     unsigned *sync;
     DecodeState *host;  // pinned
     TcmTop2 *host_log;  // pinned
-    cudaGraphExec_t graph;
+    cudaGraphExec_t graph;      // the whole-token graph
     bool graph_ready;
     bool after_host;  // the last stream operation was a host copy: next launch is not programmatic
     unsigned long long *trace;  // timeline buffer (kTraceLaunches x kTraceCtas x 4) or null
     int trace_next;
     int grid, launches;
+    unsigned *sched;            // row-group counters, two per launch site (layer * 5 + stage; readout last)
     bool ring_on;               // cache-callback layers are served by `ring`
     QwenB200Ring ring;
     QwenB200RingStep staged;    // written with the next token state
@@ -737,6 +741,9 @@ unsigned long long *trace_slot(QwenB200Runner *r) {
 }
 
 bool has_dense(const QwenB200Runner *r, int layer) { return r->slots[layer] >= 0; }
+// The counter pair of a launch site. A kernel takes row groups from its pair
+// before its dependency wait, so no two launches of one token may share one.
+unsigned *sched_slot(const QwenB200Runner *r, int layer, int stage) { return r->sched + 2 * (layer * 5 + stage); }
 size_t slot_offset(const QwenB200Runner *r, int layer) {
     const QwenB200Shape &s = r->d->s;
     return (size_t)r->slots[layer] * s.kvheads * r->b.capacity * s.head;
@@ -813,7 +820,8 @@ template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl)
 }
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Layer &L = r->d->layers[layer];
-    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, r->st, trace_slot(r), r->d->s.epsilon};
+    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, r->st, trace_slot(r), sched_slot(r, layer, 3),
+                    r->d->s.epsilon};
     launch(gateup_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
 }
 template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) {
@@ -829,7 +837,7 @@ template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl) {
 template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
     const QwenB200Decoder *d = r->d;
     ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, trace_slot(r),
-                     r->log, d->s.vocab, d->s.epsilon};
+                     r->log, sched_slot(r, d->s.layers, 0), d->s.vocab, d->s.epsilon};
     launch(readout_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
            a);
 }
@@ -859,6 +867,12 @@ bool all_dense(const QwenB200Runner *r) {
 // Every layer has a fused attention: a dense slot, or the attached ring.
 bool all_served(const QwenB200Runner *r) { return r->ring_on || all_dense(r); }
 
+void drop_graphs(QwenB200Runner *r) {
+    if (r->graph_ready) {
+        TCM_CUDA(cudaGraphExecDestroy(r->graph));
+        r->graph_ready = false;
+    }
+}
 int ensure_graph(QwenB200Runner *r) {
     if (r->graph_ready) return 0;
     if (!all_served(r)) return -1;
@@ -972,6 +986,9 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid * sizeof(int));
     r->sync = (unsigned *)gpu_alloc(2 * sizeof(unsigned));
     gpu_zero(r->sync, 2 * sizeof(unsigned));
+    const size_t sched_bytes = (size_t)(d->s.layers * 5 + 1) * 2 * sizeof(unsigned);
+    r->sched = (unsigned *)gpu_alloc(sched_bytes);
+    gpu_zero(r->sched, sched_bytes);
     TCM_CUDA(cudaMallocHost((void **)&r->host, sizeof(DecodeState)));
     TCM_CUDA(cudaMallocHost((void **)&r->host_log, kLogCap * sizeof(TcmTop2)));
     r->launches = d->s.layers * 5 + 1;
@@ -981,7 +998,7 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
 void qwen_b200_runner_free(QwenB200Runner *r) {
     if (!r) return;
     TCM_CUDA(cudaStreamSynchronize(stream()));
-    if (r->graph_ready) TCM_CUDA(cudaGraphExecDestroy(r->graph));
+    drop_graphs(r);
     gpu_free(r->trace);
     gpu_free(r->st);
     gpu_free(r->log);
@@ -990,6 +1007,7 @@ void qwen_b200_runner_free(QwenB200Runner *r) {
     gpu_free(r->top_pv);
     gpu_free(r->top_pi);
     gpu_free(r->sync);
+    gpu_free(r->sched);
     TCM_CUDA(cudaFreeHost(r->host));
     TCM_CUDA(cudaFreeHost(r->host_log));
     delete r;
@@ -1057,10 +1075,7 @@ int qwen_b200_ring_attach(QwenB200Runner *r, const QwenB200Ring *g) {
         g->positions < 1 || g->positions > r->d->s.max_position || ((uintptr_t)g->arena & 15))
         return -1;
     TCM_CUDA(cudaStreamSynchronize(stream()));
-    if (r->graph_ready) {
-        TCM_CUDA(cudaGraphExecDestroy(r->graph));
-        r->graph_ready = false;
-    }
+    drop_graphs(r);
     r->ring = *g;
     r->ring_on = true;
     r->staged = QwenB200RingStep{};
@@ -1129,10 +1144,7 @@ int qwen_b200_launches_per_token(const QwenB200Runner *r) { return r ? r->launch
 int qwen_b200_trace(QwenB200Runner *r, int enable) {
     if (!r) return -1;
     TCM_CUDA(cudaStreamSynchronize(stream()));
-    if (r->graph_ready) {
-        TCM_CUDA(cudaGraphExecDestroy(r->graph));
-        r->graph_ready = false;
-    }
+    drop_graphs(r);
     if (r->trace) {
         gpu_free(r->trace);
         r->trace = nullptr;

@@ -127,6 +127,51 @@ __device__ __forceinline__ void ring_produce(const Ring &r, int items, int per_s
         if (!mbar_wait(&r.full[g % r.stages], (g / r.stages) & 1, err, kErrDrain)) break;
 }
 
+// Dynamic variant: row groups are taken from a global counter (cnt[0]; cnt[1]
+// counts finished producers and the last one resets both), so the CTAs that
+// stream fastest take more groups and all finish together. Each stage carries
+// its group in hdr[stage]; a stage with group -1 (no data) ends the stream.
+// The next group's index is fetched while the current stage's wait runs.
+template <typename SrcFn>
+__device__ __forceinline__ void ring_produce_dynamic(const Ring &r, int items, int per_stage, uint32_t item_bytes,
+                                                     SrcFn src, unsigned *cnt, int *hdr, unsigned *err) {
+    const int groups = (items + per_stage - 1) / per_stage;
+    int g = 0;
+    int next = (int)atomicAdd(&cnt[0], 1u);
+    for (;; g++) {
+        const int grp = next;
+        const bool done = grp >= groups;
+        if (!done) next = (int)atomicAdd(&cnt[0], 1u);
+        const int s = g % r.stages;
+        if (g >= r.stages && !mbar_wait(&r.empty[s], ((g / r.stages) & 1) ^ 1, err, kErrEmptyWait)) break;
+        hdr[s] = done ? -1 : grp;
+        if (done) {
+            mbar_arrive(&r.full[s]);  // the end marker: no data
+            g++;                      // counted, so the drain sees every stage's latest phase
+            break;
+        }
+        const int first = grp * per_stage, n = min(per_stage, items - first);
+        mbar_expect_tx(&r.full[s], (uint32_t)n * item_bytes);
+        for (int j = 0; j < n; j++) bulk_copy_g2s(r.stage(s) + (size_t)j * item_bytes, src(first + j), item_bytes, &r.full[s]);
+    }
+    for (int d = g > r.stages ? g - r.stages : 0; d < g; d++)
+        if (!mbar_wait(&r.full[d % r.stages], (d / r.stages) & 1, err, kErrDrain)) break;
+    __threadfence();
+    if (atomicAdd(&cnt[1], 1u) == gridDim.x - 1) {
+        cnt[0] = 0u;
+        cnt[1] = 0u;
+    }
+}
+// Consumer side of the dynamic ring: wait for stage g; returns its group, or -1
+// at the end of the stream or when the wait ran out (*failed set).
+__device__ __forceinline__ int ring_next(const Ring &r, int g, const int *hdr, unsigned *err, bool *failed) {
+    if (!mbar_wait(&r.full[g % r.stages], (g / r.stages) & 1, err, kErrFullWait)) {
+        *failed = true;
+        return -1;
+    }
+    return hdr[g % r.stages];
+}
+
 // Consumer side: wait for group g's stage; release it (one arrive per warp).
 __device__ __forceinline__ bool ring_acquire(const Ring &r, int g, unsigned *err) {
     return mbar_wait(&r.full[g % r.stages], (g / r.stages) & 1, err, kErrFullWait);
