@@ -525,6 +525,8 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
     assert status == 0
     p0, pos0, window = s.pending, s.position, cfg["window"]
     runner = s.runner
+    if args.token_mode == "persistent":
+        assert s.persistent(1) == 1
     per_token_launches = L.qwen_b200_launches_per_token(runner)
 
     def enqueue_steps(k):
@@ -593,7 +595,7 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
         "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16-weights/f32" if es == 2 else "f32", "data": "synthetic",
         "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": shape.layers, "batch": 1,
-                   "prompt_tokens": cfg["prompt"], "decode_window": window,
+                   "prompt_tokens": cfg["prompt"], "decode_window": window, "token_execution": args.token_mode,
                    "weights": "seeded N(0,0.02) random init", "parallelism": f"replicas{world}",
                    "l2": "inputs larger than L2 (weights stream from HBM every step)"},
         "e2e": {"value": round(args.steps * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
@@ -621,6 +623,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="fp32-ctx512")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--token-mode", choices=["graph", "persistent"], default="graph",
+                    help="batch-1 whole-token execution: the per-stage token graph or the persistent kernel")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
 

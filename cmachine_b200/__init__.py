@@ -137,6 +137,8 @@ def _declare(L, strict: bool = True):
         # include/qwen_b200.h
         "qwen_b200_decoder_weight_bytes": (c_size_t, [P]),
         "qwen_b200_launches_per_token": (c_int, [P]),
+        "qwen_b200_persistent": (c_int, [P, c_int]),
+        "qwen_b200_persistent_tune": (c_int, [P, c_int, c_int]),
         "qwen_b200_time_stage": (c_float, [P, c_int, c_int, c_int, c_int]),
         "qwen_b200_trace": (c_int, [P, c_int]),
         "qwen_b200_trace_read": (c_int, [P, P, c_size_t]),
@@ -355,6 +357,10 @@ class Session:
 
     @property
     def runner(self): return self.L.qwen_b200_session_runner(self.handle)
+
+    def persistent(self, mode: int = -1) -> int:
+        """Whole-token execution of the fused runner: 1 persistent kernel, 0 token graph, -1 query."""
+        return self.L.qwen_b200_persistent(self.runner, mode)
 
     def free(self):
         if self._live:

@@ -72,12 +72,14 @@ __device__ __forceinline__ void state_merge(float (&m)[G], float (&l)[G], float4
 }
 // Merge the eight warps' states in warp order; write a partial (m, l, acc) to
 // `partial`, or the normalised result acc / l to `out` ([G][128]).
-template <int G>
+// `sync` is a barrier over the eight warps (the CTA's, or a named barrier when
+// the CTA has other warps).
+template <int G, class Sync>
 __device__ __forceinline__ void cta_merge(const float (&m)[G], const float (&l)[G], const float4 (&acc)[G],
                                           float (*wm)[G], float (*wl)[G], float (*wacc)[G][kHeadDim], float *partial,
-                                          float *out) {
+                                          float *out, Sync sync) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __syncthreads();  // the buffers may still be read by a previous merge
+    sync();  // the buffers may still be read by a previous merge
 #pragma unroll
     for (int g = 0; g < G; g++) {
         reinterpret_cast<float4 *>(wacc[warp][g])[lane] = acc[g];
@@ -86,7 +88,7 @@ __device__ __forceinline__ void cta_merge(const float (&m)[G], const float (&l)[
             wl[warp][g] = l[g];
         }
     }
-    __syncthreads();
+    sync();
     for (int o = tid; o < G * kHeadDim; o += kDecodeAttnThreads) {
         const int g = o / kHeadDim, d = o % kHeadDim;
         float M = -INFINITY;
@@ -248,20 +250,93 @@ struct ByteRows {
     __device__ __forceinline__ float bias(int t) const { return (weighted && t >= na && t < na + nm) ? bias_v : 0.f; }
 };
 
+// One flash-decoding step of a warp over four rows: k4[i], v4[i] hold the
+// lane's four dimensions of row i, rows i >= nvalid are padding (K and V
+// zero), bias(i) is row i's additive score term (kBias only). The partial dots
+// of the 4 x 8 (row, head) pairs (heads padded to eight) go through a
+// reduce-scatter butterfly: after the stage with offset o each lane keeps the
+// half of its values selected by bit o of its lane id, so 31 shuffles leave
+// lane j = 8 * row + head with the full dot of its pair. The lanes with
+// lane % 8 == g keep head g's running max m_run and rescaled sum l_run; acc
+// holds the lane's four dimensions of every head. Every product is an
+// explicit, uncontracted operation, so two kernels that run the same steps on
+// the same rows produce the same bits.
+template <int G, bool kBias, class BiasFn>
+__device__ __forceinline__ void flash_step(const float4 (&q4)[G], const float4 (&k4)[4], const float4 (&v4)[4],
+                                           int nvalid, int lane, float inv_sqrt_dim, BiasFn bias, float &m_run,
+                                           float &l_run, float4 (&acc)[G]) {
+    constexpr int GP = 8;     // padded heads: 4 rows x 8 heads = 32 scores, one per lane
+    constexpr int kStep = 4;  // rows per step
+    const int my_row = lane >> 3, my_head = lane & 7;
+    float v[kStep * GP];
+#pragma unroll
+    for (int i = 0; i < kStep; i++)
+#pragma unroll
+        for (int g = 0; g < GP; g++) {
+            if (g < G) {
+                float d = __fmul_rn(q4[g].x, k4[i].x);
+                d = fmaf(q4[g].y, k4[i].y, d);
+                d = fmaf(q4[g].z, k4[i].z, d);
+                v[GP * i + g] = fmaf(q4[g].w, k4[i].w, d);
+            } else {
+                v[GP * i + g] = 0.f;
+            }
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < o; j++) {
+            const float send = upper ? v[j] : v[j + o];
+            const float keep = upper ? v[j + o] : v[j];
+            v[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+        }
+    }
+    const bool valid = my_row < nvalid && my_head < G;
+    float sc;
+    if constexpr (kBias) {
+        // (score + bias) / sqrt(128): the reference adds the bias before the
+        // softmax scales (src/qwen_cache.inc:34, src/qwen_cuda.cu:67).
+        sc = valid ? __fmul_rn(__fadd_rn(v[0], bias(my_row)), inv_sqrt_dim) : -INFINITY;
+    } else {
+        sc = valid ? __fmul_rn(v[0], inv_sqrt_dim) : -INFINITY;
+    }
+    float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float m_new = fmaxf(m_run, mx);
+    const float c = m_run == -INFINITY ? 0.f : expf(__fsub_rn(m_run, m_new));
+    const float p = sc == -INFINITY ? 0.f : expf(__fsub_rn(sc, m_new));
+    float ps = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 8));
+    ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, 16));
+    l_run = fmaf(l_run, c, ps);
+    m_run = m_new;
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float cg_ = __shfl_sync(0xffffffffu, c, g);
+        float4 a = make_float4(__fmul_rn(acc[g].x, cg_), __fmul_rn(acc[g].y, cg_), __fmul_rn(acc[g].z, cg_),
+                               __fmul_rn(acc[g].w, cg_));
+#pragma unroll
+        for (int i = 0; i < kStep; i++) {
+            const float pg = __shfl_sync(0xffffffffu, p, GP * i + g);
+            a.x = fmaf(pg, v4[i].x, a.x);
+            a.y = fmaf(pg, v4[i].y, a.y);
+            a.z = fmaf(pg, v4[i].z, a.z);
+            a.w = fmaf(pg, v4[i].w, a.w);
+        }
+        acc[g] = a;
+    }
+}
+
 // One warp's flash-decoding over rows [r0, r1) of `rows` for the G query
-// heads whose 4 dimensions per lane are in q4: four rows per step (the next
-// step's rows loaded ahead), a reduce-scatter butterfly leaving lane
-// (row i = lane / 8, head g = lane % 8) with one score, the running max and
-// sum of head g kept in the lanes with lane % 8 == g. Returns the warp's state
-// in (m[G], l[G], acc[G]) (every lane holds m and l of every head).
+// heads whose 4 dimensions per lane are in q4: four rows per step from r0 on
+// (the next step's rows loaded ahead). Returns the warp's state in
+// (m[G], l[G], acc[G]) (every lane holds m and l of every head).
 template <int G, class Rows>
 __device__ __forceinline__ void flash_rows(const Rows &rows, int r0, int r1, const float4 (&q4)[G], int lane,
                                            float inv_sqrt_dim, float (&m)[G], float (&l)[G], float4 (&acc)[G]) {
-    constexpr int GP = 8;       // padded heads: 4 rows x 8 heads = 32 scores, one per lane
-    constexpr int kStep = 4;    // rows per step
+    constexpr int kStep = 4;
 #pragma unroll
     for (int g = 0; g < G; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int my_row = lane >> 3, my_head = lane & 7;
     float m_run = -INFINITY, l_run = 0.f;
     float4 k4[kStep], v4[kStep], nk4[kStep], nv4[kStep];
     auto load_rows = [&](int t, float4 (&kk)[kStep], float4 (&vv)[kStep]) {
@@ -278,66 +353,8 @@ __device__ __forceinline__ void flash_rows(const Rows &rows, int r0, int r1, con
     if (r0 < r1) load_rows(r0, k4, v4);
     for (int t = r0; t < r1; t += kStep) {
         if (t + kStep < r1) load_rows(t + kStep, nk4, nv4);
-        // Partial dots for the 32 (row, head) pairs, then a reduce-scatter
-        // butterfly: after the stage with offset o each lane keeps the half of
-        // its values selected by bit o of its lane id, so 31 shuffles leave
-        // lane j holding the full dot of pair j.
-        float v[kStep * GP];
-#pragma unroll
-        for (int i = 0; i < kStep; i++)
-#pragma unroll
-            for (int g = 0; g < GP; g++) {
-                if (g < G) {
-                    float d = q4[g].x * k4[i].x;
-                    d = fmaf(q4[g].y, k4[i].y, d);
-                    d = fmaf(q4[g].z, k4[i].z, d);
-                    v[GP * i + g] = fmaf(q4[g].w, k4[i].w, d);
-                } else {
-                    v[GP * i + g] = 0.f;
-                }
-            }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int j = 0; j < o; j++) {
-                const float send = upper ? v[j] : v[j + o];
-                const float keep = upper ? v[j + o] : v[j];
-                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
-        const bool valid = t + my_row < r1 && my_head < G;
-        float sc;
-        if constexpr (Rows::kBias) {
-            // (score + bias) / sqrt(128): the reference adds the bias before
-            // the softmax scales (src/qwen_cache.inc:34, src/qwen_cuda.cu:67).
-            sc = valid ? __fmul_rn(__fadd_rn(v[0], rows.bias(t + my_row)), inv_sqrt_dim) : -INFINITY;
-        } else {
-            sc = valid ? v[0] * inv_sqrt_dim : -INFINITY;
-        }
-        float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float m_new = fmaxf(m_run, mx);
-        const float c = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
-        const float p = sc == -INFINITY ? 0.f : expf(sc - m_new);
-        float ps = p + __shfl_xor_sync(0xffffffffu, p, 8);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-        l_run = fmaf(l_run, c, ps);
-        m_run = m_new;
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float cg_ = __shfl_sync(0xffffffffu, c, g);
-            float4 a = make_float4(acc[g].x * cg_, acc[g].y * cg_, acc[g].z * cg_, acc[g].w * cg_);
-#pragma unroll
-            for (int i = 0; i < kStep; i++) {
-                const float pg = __shfl_sync(0xffffffffu, p, GP * i + g);
-                a.x = fmaf(pg, v4[i].x, a.x);
-                a.y = fmaf(pg, v4[i].y, a.y);
-                a.z = fmaf(pg, v4[i].z, a.z);
-                a.w = fmaf(pg, v4[i].w, a.w);
-            }
-            acc[g] = a;
-        }
+        flash_step<G, Rows::kBias>(q4, k4, v4, r1 - t, lane, inv_sqrt_dim, [&](int i) { return rows.bias(t + i); },
+                                   m_run, l_run, acc);
 #pragma unroll
         for (int i = 0; i < kStep; i++) {
             k4[i] = nk4[i];
@@ -406,7 +423,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     if (mark && tid == 0) mark[2] = attn_clock();
     // This CTA's slice result into shared memory, then the cluster combine:
     // rank r folds the cluster's partials for outputs [r * kOutPer, ...).
-    cta_merge<G>(m, l, acc, wm, wl, wacc, cta_part, nullptr);
+    cta_merge<G>(m, l, acc, wm, wl, wacc, cta_part, nullptr, [] { __syncthreads(); });
     cluster.sync();
     constexpr int kOutPer = G * kHeadDim / kCluster;
     static_assert(G * kHeadDim % kCluster == 0 && kOutPer <= kDecodeAttnThreads, "cluster output split");

@@ -14,6 +14,8 @@
 #include "attention.cuh"
 #include "attention_decode.cuh"
 #include "stream.cuh"
+#include "lanes.cuh"
+#include "persistent.cuh"
 #include "kernels.h"
 #include "../../include/qwen_b200.h"
 #include "../../include/tcm_seeded.h"
@@ -22,130 +24,7 @@
 
 namespace tcm {
 
-// Device-resident token state: the host writes token/position before a token;
-// the readout's last CTA publishes the top-2 and, for chained greedy decode,
-// feeds top-1 back as the next token and advances the position. `fault`
-// collects the bits of any pipeline wait that ran out.
-// Bits of `invalid`: 1 non-finite logits, 2 a non-finite K/V row encoded into
-// a ring arena. `ring` is the token's ring bookkeeping (ring layers only).
-struct DecodeState {
-    int token, position, step, invalid;
-    unsigned fault;
-    int pad[3];
-    TcmTop2 top;
-    QwenB200RingStep ring;
-};
-constexpr int kLogCap = 4096;
-constexpr int kRingRowBytes = 528;  // one ring row: 4 x 128 codes + 4 FP32 scales
-
 namespace {
-
-constexpr int kHidden = 1536;       // Qwen2.5-1.5B hidden size (the fused kernels' geometry)
-constexpr int kInter = 8960;        // MLP width
-constexpr int kMaxPairsPerCta = 64; // q/k/v row pairs one CTA may own
-
-// Weight geometry: E elements per 16-byte vector; R rows of 1536 per stage
-// (48 KB either way); RD rows of 8960 per down stage (35 KB).
-template <typename WT> struct Geo;
-template <> struct Geo<float> { static constexpr int E = 4, R = 8, RD = 1; };
-template <> struct Geo<uint16_t> { static constexpr int E = 8, R = 16, RD = 2; };
-template <typename WT> constexpr int kNV = kHidden / (32 * Geo<WT>::E);  // vectors per lane in a row of 1536
-template <typename WT> constexpr uint32_t kRow = kHidden * sizeof(WT);
-template <typename WT> constexpr uint32_t kStage = Geo<WT>::R * kRow<WT>;
-template <typename WT> constexpr uint32_t kDownRow = kInter * sizeof(WT);
-template <typename WT> constexpr uint32_t kDownStage = Geo<WT>::RD * kDownRow<WT>;
-constexpr int kStages = 2, kDownStages = 3;
-constexpr int kLaneX = 48;  // floats of a 1536-vector one lane holds
-
-// ---------------------------------------------------------------- lane-resident vectors
-// Lane layout of a 1536-vector: lane owns 16-byte weight vectors v = lane + 32k
-// (k < kNV), i.e. elements E*v .. E*v+E-1, stored at xr[E*k ...].
-template <typename WT> __device__ __forceinline__ void load_lane_vec(float (&xr)[kLaneX], const float *x, int lane) {
-    constexpr int E = Geo<WT>::E;
-#pragma unroll
-    for (int k = 0; k < kNV<WT>; k++)
-#pragma unroll
-        for (int h = 0; h < E / 4; h++) {
-            const float4 f = reinterpret_cast<const float4 *>(x)[(E / 4) * (lane + 32 * k) + h];
-            xr[E * k + 4 * h] = f.x;
-            xr[E * k + 4 * h + 1] = f.y;
-            xr[E * k + 4 * h + 2] = f.z;
-            xr[E * k + 4 * h + 3] = f.w;
-        }
-}
-template <typename WT> __device__ __forceinline__ void store_lane_vec(float *x, const float (&xr)[kLaneX], int lane) {
-    constexpr int E = Geo<WT>::E;
-#pragma unroll
-    for (int k = 0; k < kNV<WT>; k++)
-#pragma unroll
-        for (int h = 0; h < E / 4; h++)
-            reinterpret_cast<float4 *>(x)[(E / 4) * (lane + 32 * k) + h] =
-                make_float4(xr[E * k + 4 * h], xr[E * k + 4 * h + 1], xr[E * k + 4 * h + 2], xr[E * k + 4 * h + 3]);
-}
-// A weight row (FP32 or BF16) of 1536 into the lane layout, widened to FP32.
-template <typename WT> __device__ __forceinline__ void load_lane_row(float (&xr)[kLaneX], const WT *row, int lane) {
-    if constexpr (sizeof(WT) == 4) {
-        load_lane_vec<float>(xr, reinterpret_cast<const float *>(row), lane);
-    } else {
-#pragma unroll
-        for (int k = 0; k < kNV<WT>; k++) {
-            const uint4 w = reinterpret_cast<const uint4 *>(row)[lane + 32 * k];
-            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                xr[8 * k + 2 * j] = bf16_lo(u[j]);
-                xr[8 * k + 2 * j + 1] = bf16_hi(u[j]);
-            }
-        }
-    }
-}
-// x <- (x * r) * w with r = 1 / sqrt(mean(x^2) + eps) over the whole warp's
-// vector; w is the norm weight vector staged in shared memory.
-template <typename WT> __device__ __forceinline__ void rms_lane(float (&xr)[kLaneX], const float *w_s, float eps, int lane) {
-    constexpr int E = Geo<WT>::E;
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < kLaneX; i++) ss = fmaf(xr[i], xr[i], ss);
-    ss = warp_sum(ss);
-    const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHidden), eps)));
-#pragma unroll
-    for (int k = 0; k < kNV<WT>; k++)
-#pragma unroll
-        for (int j = 0; j < E; j++)
-            xr[E * k + j] = __fmul_rn(__fmul_rn(xr[E * k + j], r), w_s[E * (lane + 32 * k) + j]);
-}
-// The norm weights into shared memory (consumer threads; before the wait).
-__device__ __forceinline__ void stage_norm(float *w_s, const float *w) {
-    for (int i = threadIdx.x; i < kHidden / 4; i += kConsumerWarps * 32)
-        reinterpret_cast<float4 *>(w_s)[i] = reinterpret_cast<const float4 *>(w)[i];
-}
-__device__ __forceinline__ float dot_vec(const uint4 &w, const float *x, float acc, float) {
-    acc = fmaf(__uint_as_float(w.x), x[0], acc);
-    acc = fmaf(__uint_as_float(w.y), x[1], acc);
-    acc = fmaf(__uint_as_float(w.z), x[2], acc);
-    return fmaf(__uint_as_float(w.w), x[3], acc);
-}
-__device__ __forceinline__ float dot_vec(const uint4 &w, const float *x, float acc, uint16_t) {
-    acc = fmaf(bf16_lo(w.x), x[0], acc);
-    acc = fmaf(bf16_hi(w.x), x[1], acc);
-    acc = fmaf(bf16_lo(w.y), x[2], acc);
-    acc = fmaf(bf16_hi(w.y), x[3], acc);
-    acc = fmaf(bf16_lo(w.z), x[4], acc);
-    acc = fmaf(bf16_hi(w.z), x[5], acc);
-    acc = fmaf(bf16_lo(w.w), x[6], acc);
-    return fmaf(bf16_hi(w.w), x[7], acc);
-}
-// Warp dot product of a shared-memory row of 1536 with the lane-resident vector.
-template <typename WT> __device__ __forceinline__ float row_dot(const unsigned char *srow, const float (&xr)[kLaneX], int lane) {
-    const uint4 *v = reinterpret_cast<const uint4 *>(srow);
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < kNV<WT>; k++) acc = dot_vec(v[lane + 32 * k], &xr[Geo<WT>::E * k], acc, WT());
-    return warp_sum(acc);
-}
-
-
-__device__ __forceinline__ int share_begin(int total, int part, int parts) { return (int)((long long)part * total / parts); }
 
 // Optional timeline trace: thread 0 of each CTA stamps the global timer at
 // entry (0), when griddepcontrol.wait returned (1), when the input vector is
@@ -644,6 +523,9 @@ __global__ void set_state_kernel(DecodeState *st, int token, int position) {
     st->step = 0;
     st->invalid = 0;
     st->fault = 0u;
+    st->bar = 0u;
+    st->arrive = 0u;
+    st->nonfinite = 0u;
 }
 
 template <typename T> inline void set_smem(T *kernel, size_t bytes) {
@@ -697,6 +579,10 @@ struct QwenB200Runner {
     bool ring_on;               // cache-callback layers are served by `ring`
     QwenB200Ring ring;
     QwenB200RingStep staged;    // written with the next token state
+    PersistLayer *pers_layers;  // device copy of the layers for the persistent token kernel
+    float *pers_part;           // its attention partials
+    bool persistent;            // whole tokens run as one persistent launch (when eligible)
+    unsigned lookahead;         // its per-CTA L2 prefetch distance (bytes)
 };
 
 int tcm::decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
@@ -734,6 +620,7 @@ void setup_kernels() {
 }
 
 constexpr int kTraceLaunches = 160, kTraceCtas = 160;
+constexpr unsigned kDefaultLookahead = 0u;  // persistent kernel: L2 prefetch distance per CTA (measured: no gain)
 // The trace slot of the next launch (launch order within a token), or null.
 unsigned long long *trace_slot(QwenB200Runner *r) {
     if (!r->trace) return nullptr;
@@ -867,6 +754,53 @@ bool all_dense(const QwenB200Runner *r) {
 // Every layer has a fused attention: a dense slot, or the attached ring.
 bool all_served(const QwenB200Runner *r) { return r->ring_on || all_dense(r); }
 
+// The persistent token kernel serves the runner: every layer has a dense cache
+// slot, no ring is attached, the attention split and the barrier timestamps
+// fit the grid, and one CTA fits an SM.
+int ensure_graph(QwenB200Runner *r);
+bool persistent_ok(const QwenB200Runner *r) {
+    const QwenB200Shape &s = r->d->s;
+    return r->pers_layers && !r->ring_on && all_dense(r) && s.kvheads * kPersistAttnCtasPerHead <= r->grid &&
+           12 * s.layers + 2 <= kPersistMarks && (size_t)r->grid * kPersistMarks <= (size_t)kTraceLaunches * kTraceCtas * 4 &&
+           persistent_blocks_per_sm(r->d->dtype) >= 1;
+}
+bool use_persistent(const QwenB200Runner *r) { return r->persistent && persistent_ok(r); }
+void launch_persistent_token(QwenB200Runner *r) {
+    const QwenB200Decoder *d = r->d;
+    const QwenB200Shape &s = d->s;
+    PersistArgs a = {};
+    a.layers = r->pers_layers;
+    a.embed = d->embed;
+    a.final_norm = d->norm;
+    a.rope_den = d->rope_den;
+    a.x = r->b.x; a.q = r->b.q; a.k = r->b.k; a.v = r->b.v;
+    a.attn = r->b.attention; a.h = r->b.gate; a.logits = r->b.logits;
+    a.part = r->pers_part;
+    a.pv = r->top_pv;
+    a.pi = r->top_pi;
+    a.st = r->st;
+    a.log = r->log;
+    a.trace = r->trace;  // [grid][kPersistMarks] while the persistent kernel serves the runner
+    a.nlayers = s.layers; a.qheads = s.qheads; a.kvheads = s.kvheads;
+    a.capacity = r->b.capacity; a.vocab = s.vocab;
+    a.eps = s.epsilon;
+    a.inv_sqrt_dim = 1.0f / sqrtf((float)kHeadDim);
+    a.lookahead = r->lookahead;
+    launch_persistent(d->dtype, a, r->grid, stream());
+    r->after_host = true;
+}
+// One whole token: the persistent launch, or the token graph.
+int run_token(QwenB200Runner *r) {
+    if (use_persistent(r)) {
+        launch_persistent_token(r);
+        return 0;
+    }
+    if (ensure_graph(r)) return -1;
+    TCM_CUDA(cudaGraphLaunch(r->graph, stream()));
+    r->after_host = true;
+    return 0;
+}
+
 void drop_graphs(QwenB200Runner *r) {
     if (r->graph_ready) {
         TCM_CUDA(cudaGraphExecDestroy(r->graph));
@@ -893,6 +827,9 @@ void write_state(QwenB200Runner *r, int token, int position) {
     r->host->step = 0;
     r->host->invalid = 0;
     r->host->fault = 0u;
+    r->host->bar = 0u;
+    r->host->arrive = 0u;
+    r->host->nonfinite = 0u;
     r->host->ring = r->staged;
     // With a ring the whole state goes (the step follows the top-2 field).
     const size_t bytes = r->ring_on ? sizeof(DecodeState) : 8 * sizeof(int);
@@ -992,6 +929,18 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     TCM_CUDA(cudaMallocHost((void **)&r->host, sizeof(DecodeState)));
     TCM_CUDA(cudaMallocHost((void **)&r->host_log, kLogCap * sizeof(TcmTop2)));
     r->launches = d->s.layers * 5 + 1;
+    std::vector<PersistLayer> pl(d->s.layers);
+    for (int l = 0; l < d->s.layers; l++) {
+        const QwenB200Layer &L = d->layers[l];
+        const bool dense = r->slots[l] >= 0;
+        pl[l] = PersistLayer{L.q, L.k, L.v, L.o, L.gate, L.up, L.down, L.qb, L.kb, L.vb, L.input_norm, L.post_norm,
+                             dense ? b->keys + slot_offset(r, l) : nullptr, dense ? b->values + slot_offset(r, l) : nullptr};
+    }
+    r->pers_layers = (PersistLayer *)gpu_alloc(pl.size() * sizeof(PersistLayer));
+    gpu_write(r->pers_layers, pl.data(), pl.size() * sizeof(PersistLayer));
+    r->pers_part = (float *)gpu_alloc((size_t)d->s.kvheads * kPersistAttnCtasPerHead * kAttnPartialFloats * sizeof(float));
+    r->persistent = false;  // the token graph measured faster on B200 (persistent kernel: opt-in)
+    r->lookahead = kDefaultLookahead;
     return r;
 }
 
@@ -1008,6 +957,8 @@ void qwen_b200_runner_free(QwenB200Runner *r) {
     gpu_free(r->top_pi);
     gpu_free(r->sync);
     gpu_free(r->sched);
+    gpu_free(r->pers_layers);
+    gpu_free(r->pers_part);
     TCM_CUDA(cudaFreeHost(r->host));
     TCM_CUDA(cudaFreeHost(r->host_log));
     delete r;
@@ -1053,17 +1004,14 @@ int qwen_b200_finish(QwenB200Runner *r, TcmTop2 *top) {
 }
 
 int qwen_b200_token(QwenB200Runner *r, int token, int position, TcmTop2 *top) {
-    if (!r || !valid_token(r, token, position) || ensure_graph(r)) return -1;
+    if (!r || !valid_token(r, token, position) || (!use_persistent(r) && ensure_graph(r))) return -1;
     start_token(r, token, position);
-    TCM_CUDA(cudaGraphLaunch(r->graph, stream()));
-    r->after_host = true;
+    if (run_token(r)) return -1;
     return read_top(r, top);
 }
 
 int qwen_b200_complete(QwenB200Runner *r, TcmTop2 *top) {
-    if (!r || ensure_graph(r)) return -1;
-    TCM_CUDA(cudaGraphLaunch(r->graph, stream()));
-    r->after_host = true;
+    if (!r || run_token(r)) return -1;
     return read_top(r, top);
 }
 
@@ -1117,12 +1065,12 @@ int qwen_b200_ring_status(QwenB200Runner *r) {
 
 int qwen_b200_enqueue(QwenB200Runner *r, int token, int position, int n) {
     if (!r || r->ring_on || n < 1 || n > kLogCap || !valid_token(r, token, position) || position + n > r->b.capacity ||
-        ensure_graph(r))
+        (!use_persistent(r) && ensure_graph(r)))
         return -1;
     set_state_kernel<<<1, 1, 0, stream()>>>(r->st, token, position);
     TCM_CUDA(cudaGetLastError());
     r->after_host = true;
-    for (int i = 0; i < n; i++) TCM_CUDA(cudaGraphLaunch(r->graph, stream()));
+    for (int i = 0; i < n; i++) run_token(r);
     return 0;
 }
 
@@ -1139,7 +1087,24 @@ int qwen_b200_generate(QwenB200Runner *r, int token, int position, int n, int *i
     return status;
 }
 
-int qwen_b200_launches_per_token(const QwenB200Runner *r) { return r ? r->launches : 0; }
+int qwen_b200_launches_per_token(const QwenB200Runner *r) { return r ? (use_persistent(r) ? 1 : r->launches) : 0; }
+
+int qwen_b200_persistent_tune(QwenB200Runner *r, int key, int value) {
+    if (!r || key != 0 || value < 0 || value > 2048) return -1;
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    r->lookahead = (unsigned)value << 10;
+    return 0;
+}
+
+int qwen_b200_persistent(QwenB200Runner *r, int mode) {
+    if (!r || mode < -1 || mode > 1) return -1;
+    if (mode >= 0) {
+        if (mode == 1 && !persistent_ok(r)) return -1;
+        TCM_CUDA(cudaStreamSynchronize(stream()));
+        r->persistent = mode == 1;
+    }
+    return use_persistent(r) ? 1 : 0;
+}
 
 int qwen_b200_trace(QwenB200Runner *r, int enable) {
     if (!r) return -1;

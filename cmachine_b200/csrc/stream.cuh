@@ -71,6 +71,24 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
                  "l"(src), "r"(bytes), "r"(smem_addr(bar))
                  : "memory");
 }
+// The same copy with an L2 cache policy (e.g. evict-first for rows read once).
+__device__ __forceinline__ void bulk_copy_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                                   uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Asks L2 to fetch `bytes` (multiple of 16, 16-byte aligned) from global memory.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // Named barrier among the consumer warps only (the producer warp never joins).
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
 

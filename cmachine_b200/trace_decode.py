@@ -1,9 +1,16 @@
 """Timeline of one fused decode token (qwen_b200_trace): where the time goes
-between and inside the 141 launches of a token.
+between and inside the 141 launches of a token, or between the grid barriers
+of the persistent token kernel.
 
-    python -m cmachine_b200.trace_decode --profile 0 --prompt 512 --tokens 8
+    python -m cmachine_b200.trace_decode --profile 0 --prompt 512 --tokens 8 [--mode graph|persistent]
 
-Every CTA of every launch stamps the GPU global timer at entry, when its
+Persistent kernel: every CTA stamps the GPU global timer at its start, as it
+passes each of the six grid barriers of a layer and when its readout rows are
+done. Per phase (q/k/v, attention, merge, O, gate/up, down) the report gives the
+mean over layers of the time from the previous barrier's release (its first
+CTA through) to this one's, and how far apart the CTAs passed it.
+
+Token graph: every CTA of every launch stamps the GPU global timer at entry, when its
 dependency on the previous launch was released (griddepcontrol.wait), when its
 input vector was ready and when it finished. Per stage kind the report gives the
 mean over layers of: the gap from the previous launch's last finish to this
@@ -21,6 +28,30 @@ import cmachine_b200 as cm
 
 LAUNCHES, CTAS = 160, 160
 STAGES = ["qkv", "attention", "oproj", "gateup", "down"]
+PHASES = ["qkv", "attention", "merge", "oproj", "gateup", "down"]
+MARKS = 512
+
+
+def report_persistent(buf, layers, sms):
+    t = buf[: sms * MARKS].reshape(sms, MARKS).astype(np.float64)
+    k_last = 6 * layers
+    start = t[:, 0].min()
+    arrive = [None] + [t[:, 2 * k - 1] for k in range(1, k_last + 1)]
+    passed = [t[:, 0]] + [t[:, 2 * k] for k in range(1, k_last + 1)]
+    done = t[:, 2 * k_last + 1].max()
+    print(f"persistent token: {(done - start) / 1000:.1f} us from the first CTA's start to the last readout row")
+    print(f"{'phase':10s} {'interval':>8s} {'sum':>8s} {'work':>8s} {'barrier':>8s} {'arr spread':>10s}"
+          f"   (us, mean over layers; work = previous release to the last arrival,"
+          f" barrier = last arrival to the first CTA through)")
+    for i, name in enumerate(PHASES):
+        ks = [6 * l + i + 1 for l in range(layers)]
+        interval = [passed[k].min() - passed[k - 1].min() for k in ks]
+        work = [arrive[k].max() - passed[k - 1].min() for k in ks]
+        bar = [passed[k].min() - arrive[k].max() for k in ks]
+        spread = [arrive[k].max() - arrive[k].min() for k in ks]
+        print(f"{name:10s} {np.mean(interval) / 1000:8.2f} {np.sum(interval) / 1000:8.1f} {np.mean(work) / 1000:8.2f}"
+              f" {np.mean(bar) / 1000:8.2f} {np.mean(spread) / 1000:10.2f}")
+    print(f"{'readout':10s} {(done - passed[k_last].min()) / 1000:8.2f}")
 
 
 def main():
@@ -29,6 +60,8 @@ def main():
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--mode", choices=["graph", "persistent"], default="persistent")
+    ap.add_argument("--lookahead", type=int, default=-1, help="persistent kernel L2 prefetch distance (KB)")
     args = ap.parse_args()
     L = cm.lib()
     model = cm.Model(cm.qwen_shape(args.layers, 32768), 2026, cm.BENCH_LAW, args.profile)
@@ -36,12 +69,20 @@ def main():
     for i in range(args.prompt):
         assert s.push((i * 7919 + 11) % model.shape.vocab) == 0
     runner = s.runner
+    persistent = s.persistent(1 if args.mode == "persistent" else 0) == 1
+    if persistent and args.lookahead >= 0:
+        assert L.qwen_b200_persistent_tune(runner, 0, args.lookahead) == 0
     assert L.qwen_b200_trace(runner, 1) == 0
     status, _ = s.generate(args.tokens)
     assert status == 0
     buf = np.zeros(LAUNCHES * CTAS * 4, np.uint64)
     n = L.qwen_b200_trace_read(runner, ctypes.c_void_p(buf.ctypes.data), buf.size)
     L.qwen_b200_trace(runner, 0)
+    if persistent:
+        report_persistent(buf, args.layers, L.qwen_b200_sm_count())
+        s.free()
+        model.free()
+        return
     t = buf.reshape(LAUNCHES, CTAS, 4).astype(np.float64)
     per_token = args.layers * 5 + 1
     t0 = np.min(t[0, :, 0][t[0, :, 0] > 0])

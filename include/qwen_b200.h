@@ -196,6 +196,18 @@ int qwen_b200_batch_clusters(const QwenB200Batch *, int *qkv, int *o, int *down)
 
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
+/* Whole-token execution: 1 = one persistent cooperative launch per token (one
+ * CTA per SM runs every layer and the readout, the weights streaming through
+ * grid barriers; applies when every layer is dense and no ring is attached);
+ * 0 = the token graph of per-stage kernels (the default: faster on B200 at the
+ * measured contexts); -1 queries. Both give identical bits. Returns the mode in
+ * force, or -1 (mode 1 where it does not apply). */
+int qwen_b200_persistent(QwenB200Runner *, int mode);
+/* Tuning of the persistent kernel: key 0 = how far (KB, 0..2048) each CTA's
+ * producer prefetches its coming weight and cache rows into L2 ahead of its
+ * shared-memory copies (default 0). Returns 0, or -1 for an unknown key or
+ * value. */
+int qwen_b200_persistent_tune(QwenB200Runner *, int key, int value);
 /* Measurement aid: mean device time (ms, CUDA events) of one standalone launch
  * of fused stage `stage` of `layer` (0 q/k/v, 1 attention, 2 O projection,
  * 3 gate/up, 4 down, 5 readout) at `position`, over `reps` launches. On a ring
@@ -207,7 +219,10 @@ float qwen_b200_time_stage(QwenB200Runner *, int stage, int layer, int position,
  * stamps the GPU global timer per CTA at entry, dependency release, input ready
  * and done (the whole-token graph is re-captured). trace_read copies the last
  * token's stamps, 160 launches x 160 CTAs x 4 (zero where a CTA had no work),
- * and returns the number of launches recorded. */
+ * and returns the number of launches recorded. Under the persistent kernel the
+ * buffer's first SMs x 512 entries are per CTA: its start, then for each grid
+ * barrier (six a layer: after q/k/v, attention, merge, O, gate/up, down) the
+ * moments it arrived and passed, then the end of its readout rows. */
 int qwen_b200_trace(QwenB200Runner *, int enable);
 int qwen_b200_trace_read(QwenB200Runner *, unsigned long long *host, size_t count);
 

@@ -47,6 +47,54 @@ def test_layer_by_layer_equals_graph_token(model):
     a.free(); b.free()
 
 
+def persistent_pair(model, capacity):
+    a, b = cm.Session(model, capacity), cm.Session(model, capacity)
+    assert a.persistent(1) == 1 and b.persistent(0) == 0
+    return a, b
+
+
+def test_persistent_token_equals_graph(model):
+    """One persistent launch per token and the per-stage token graph give the
+    same bits (logits, K/V, chained generation)."""
+    fresh = cm.Session(model, 64)
+    assert fresh.persistent() == 0  # the token graph by default
+    assert fresh.persistent(1) == 1
+    assert model.L.qwen_b200_launches_per_token(fresh.runner) == 1
+    fresh.free()
+    a, b = persistent_pair(model, 64)
+    for t in (5, 9, 100, 151935, 7):
+        assert a.push(t) == 0 and b.push(t) == 0
+    equal(a, b)
+    sa, ia = a.generate(20)
+    sb, ib = b.generate(20)
+    assert sa == 0 and sb == 0 and ia == ib
+    equal(a, b)
+    a.free(); b.free()
+
+
+@pytest.mark.parametrize("profile,position", [(0, 700), (0, 1500), (2, 3000)])
+def test_persistent_long_context_equals_graph(profile, position):
+    """Seeded caches beyond one attention cluster's rows (the 64-CTA split) and
+    the BF16 profile: the persistent kernel equals the graph bit for bit."""
+    m = cm.Model(cm.qwen_shape(2, 4096), 37, cm.TEST_LAW, profile)
+    a, b = persistent_pair(m, position + 40)
+    L = m.L
+    for i, s in enumerate((a, b)):
+        v = s.view()
+        count = m.shape.layers * m.shape.kvheads * v.capacity * m.shape.head
+        L.qwen_b200_seeded_fill(cm.c_void_p(v.keys), 1, 7, 500, count, 0.0, 0.5)
+        L.qwen_b200_seeded_fill(cm.c_void_p(v.values), 1, 7, 501, count, 0.0, 0.5)
+        assert L.qwen_b200_session_set_cursor(s.handle, position, 4242) == 0
+    for t in (11, 12, 13):
+        assert a.push(t) == 0 and b.push(t) == 0
+    equal(a, b)
+    sa, ia = a.generate(30)
+    sb, ib = b.generate(30)
+    assert sa == 0 and sb == 0 and ia == ib
+    equal(a, b)
+    a.free(); b.free(); m.free()
+
+
 def test_generate_equals_advance(model):
     a, b = cm.Session(model, 64), cm.Session(model, 64)
     for t in (2, 3, 4):
