@@ -21,6 +21,7 @@
 #pragma once
 #include "common.cuh"
 #include "attention.cuh"
+#include "stream.cuh"
 #include "../../include/qwen_b200.h"
 #include <cooperative_groups.h>
 
@@ -124,14 +125,25 @@ constexpr int kSingleClusterRows = 1024;  // caches up to this length use one cl
 // line of row t in L2. current() runs after the dependency wait, before the
 // first load.
 
-// Dense FP32 rows [kvheads][capacity][128]; rows 0..position.
+// Cache rows a CTA stages in shared memory before its dependency wait.
+constexpr int kStagedRows = 80;
+constexpr uint32_t kStagedBytes = 2u * kStagedRows * kHeadDim * sizeof(float);
+
+// Dense FP32 rows [kvheads][capacity][128]; rows 0..position. The rows of a
+// CTA's slice below the newest (written by earlier tokens) are bulk-copied into
+// shared memory before the dependency wait -- up to kStagedRows of them, rows
+// [s0, s1) -- while the q/k/v kernel still runs; load() reads them there.
 struct DenseRows {
     static constexpr bool kBias = false;
+    static constexpr bool kStaged = true;
     static constexpr int kLines = 4;  // 128-byte lines per row and kind
     const float *keys, *values;
     int capacity;
     const int *position;
+    unsigned *fault;                  // receives the bit of a staging wait that ran out
     const float4 *kb, *vb;
+    const float4 *ks, *vs;            // staged rows (shared memory)
+    int s0, s1;
     __device__ __forceinline__ void bind(int kvh) {
         kb = reinterpret_cast<const float4 *>(keys + (size_t)kvh * capacity * kHeadDim);
         vb = reinterpret_cast<const float4 *>(values + (size_t)kvh * capacity * kHeadDim);
@@ -145,6 +157,11 @@ struct DenseRows {
     }
     __device__ __forceinline__ void current(int, int, int) {}
     __device__ __forceinline__ void load(int t, int lane, float4 &k, float4 &v) const {
+        if (t >= s0 && t < s1) {
+            k = ks[(t - s0) * (kHeadDim / 4) + lane];
+            v = vs[(t - s0) * (kHeadDim / 4) + lane];
+            return;
+        }
         k = __ldcg(kb + (size_t)t * (kHeadDim / 4) + lane);
         v = __ldcg(vb + (size_t)t * (kHeadDim / 4) + lane);
     }
@@ -192,6 +209,7 @@ __device__ __forceinline__ float4 dequant4(unsigned w, float s) {
 // (identical bits everywhere), and CTA 0 of the head also stores it.
 struct ByteRows {
     static constexpr bool kBias = true;
+    static constexpr bool kStaged = false;
     static constexpr int kLines = 1;
     const signed char *arena;  // this layer
     int rows, anchors, reservoir_base;  // reservoir_base = anchors + recent
@@ -377,6 +395,8 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
     __shared__ __align__(16) float cta_part[kAttnPartialFloats];
     __shared__ int last_s;
+    __shared__ __align__(8) uint64_t kv_bar;
+    extern __shared__ __align__(128) unsigned char staged[];  // [K rows][V rows], kStagedRows each (DenseRows)
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     const int kvh = blockIdx.y, rank = (int)cluster.block_rank(), cid = blockIdx.x / kCluster;
@@ -402,15 +422,40 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int t0 = min(L, cta * chunk), t1 = min(L, t0 + chunk);
     const int per_warp = (t1 - t0 + kDecodeAttnWarps - 1) / kDecodeAttnWarps;
     const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
+    int stage_from = r0;  // rows below this one are staged in shared memory
+    if constexpr (Rows::kStaged) {
+        rows.s0 = t0;
+        rows.s1 = max(t0, min(min(t1, rows.prefetch_limit()), t0 + kStagedRows));
+        rows.ks = reinterpret_cast<const float4 *>(staged);
+        rows.vs = reinterpret_cast<const float4 *>(staged + kStagedBytes / 2);
+        if (tid == 0) {
+            mbar_init(&kv_bar, 1);
+            mbar_fence_init();
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t nb = (uint32_t)(rows.s1 - rows.s0) * kHeadDim * sizeof(float);
+            if (nb) {
+                mbar_expect_tx(&kv_bar, 2 * nb);
+                bulk_copy_g2s(staged, rows.kb + (size_t)rows.s0 * (kHeadDim / 4), nb, &kv_bar);
+                bulk_copy_g2s(staged + kStagedBytes / 2, rows.vb + (size_t)rows.s0 * (kHeadDim / 4), nb, &kv_bar);
+            } else {
+                mbar_arrive(&kv_bar);
+            }
+        }
+        stage_from = max(r0, rows.s1);
+    }
     {
         constexpr int kRowsPerPass = 32 / Rows::kLines;
         const int limit = min(r1, rows.prefetch_limit());
-        for (int t = r0 + lane / Rows::kLines; t < limit; t += kRowsPerPass) rows.prefetch_line(t, lane % Rows::kLines);
+        for (int t = stage_from + lane / Rows::kLines; t < limit; t += kRowsPerPass)
+            rows.prefetch_line(t, lane % Rows::kLines);
     }
     pdl_wait();
     if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
     rows.current(lane, warp, cta);
+    if constexpr (Rows::kStaged) mbar_wait(&kv_bar, 0, rows.fault, kErrFullWait);
 
     float4 q4[G], acc[G];
 #pragma unroll

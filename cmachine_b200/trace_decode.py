@@ -102,21 +102,25 @@ def main():
                    done1=done.max() if done.size else np.nan, release_spread=rel.max() - rel.min(),
                    cta_ready=np.median(m[both, 2] - m[both, 1]) if both.any() else np.nan,
                    cta_work=np.median(m[fin, 3] - m[fin, 2]) if fin.any() else np.nan,
-                   done_spread=(done.max() - done.min()) if done.size else np.nan)
+                   done_spread=(done.max() - done.min()) if done.size else np.nan,
+                   lead=np.median(m[live, 1] - m[live, 0]) if live.any() else np.nan)
         rec["boundary"] = rec["release0"] - prev_done if prev_done is not None else np.nan
         prev_done = rec["done1"]
         rows.append(rec)
     print(f"launches recorded: {n}; token span {rows[-1]['done1'] / 1000:.1f} us")
     print(f"{'stage':10s} {'boundary':>9s} {'rel->ready':>10s} {'ready->done':>11s} {'span':>8s} "
-          f"{'rel spread':>10s} {'cta ready':>9s} {'cta work':>9s} {'done spread':>11s}   (us, mean over layers)")
+          f"{'rel spread':>10s} {'cta ready':>9s} {'cta work':>9s} {'done spread':>11s} {'resident':>8s}"
+          f"   (us, mean over layers; resident = a CTA's entry to its release, median)")
     for kind in STAGES + ["readout"]:
         sel = [r for r in rows if r["kind"] == kind]
         b = np.nanmean([r["boundary"] for r in sel]) / 1000
         rr = np.nanmean([r["ready1"] - r["release0"] for r in sel]) / 1000
         rd = np.nanmean([r["done1"] - r["ready1"] for r in sel]) / 1000
         sp = np.nanmean([r["done1"] - r["release0"] for r in sel]) / 1000
-        extra = [np.nanmean([r[k] for r in sel]) / 1000 for k in ("release_spread", "cta_ready", "cta_work", "done_spread")]
-        print(f"{kind:10s} {b:9.2f} {rr:10.2f} {rd:11.2f} {sp:8.2f} {extra[0]:10.2f} {extra[1]:9.2f} {extra[2]:9.2f} {extra[3]:11.2f}")
+        extra = [np.nanmean([r[k] for r in sel]) / 1000
+                 for k in ("release_spread", "cta_ready", "cta_work", "done_spread", "lead")]
+        print(f"{kind:10s} {b:9.2f} {rr:10.2f} {rd:11.2f} {sp:8.2f} {extra[0]:10.2f} {extra[1]:9.2f} {extra[2]:9.2f}"
+              f" {extra[3]:11.2f} {extra[4]:8.2f}")
     s.free()
     model.free()
 
