@@ -519,8 +519,14 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
     model = cm.Model(shape, 2026 + rank, cm.BENCH_LAW, cfg["profile"])
     capacity = cfg["prompt"] + cfg["window"] + 1
     s = cm.Session(model, capacity)
-    for t in prompt_tokens(7 + rank, cfg["prompt"], shape.vocab):
-        assert s.push(t) == 0
+    # The prompt through qwen_prefill (batched causal tensor-core steps on a BF16
+    # model; token by token on FP32), timed on the device.
+    L.gpu_sync()
+    L.qwen_b200_mark(4)
+    assert s.prefill(prompt_tokens(7 + rank, cfg["prompt"], shape.vocab)) == 0
+    L.qwen_b200_mark(5)
+    L.gpu_sync()
+    prefill_ms = L.qwen_b200_elapsed_ms(4, 5)
     status, ckpt = s.checkpoint()
     assert status == 0
     p0, pos0, window = s.pending, s.position, cfg["window"]
@@ -609,6 +615,9 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
         "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
                           "frac": round(step_bytes / (ms_per_step * 1e6) / peak, 4)},
         "stage_ms_layer0": stage_ms,
+        "prefill": {"tokens": cfg["prompt"], "ms": round(prefill_ms, 3),
+                    "tokens_per_s": round(cfg["prompt"] / (prefill_ms * 1e-3), 1),
+                    "path": "batched tensor-core steps of 64 tokens" if es == 2 else "token by token (FP32 weights)"},
         "clocks": clocks.summary(),
         "last_top2": top.tuple(),
     }

@@ -134,6 +134,8 @@ def _declare(L, strict: bool = True):
         "qwen_generate": (c_int, [P, c_int, POINTER(c_int)]),
         "qwen_complete_token": (c_int, [P]),
         "qwen_push_batch": (c_int, [P, c_int, P]),
+        "qwen_prefill": (c_int, [P, P, c_int]),
+        "qwen_b200_batch_prefill": (c_int, [P, P, P, c_int, c_int, P]),
         # include/qwen_b200.h
         "qwen_b200_decoder_weight_bytes": (c_size_t, [P]),
         "qwen_b200_launches_per_token": (c_int, [P]),
@@ -288,6 +290,11 @@ class Session:
 
     def stack_rollback(self, frame: int) -> int: return self.L.qwen_stack_rollback(self.handle, frame)
     def stack_commit(self, frame: int) -> int: return self.L.qwen_stack_commit(self.handle, frame)
+
+    def prefill(self, tokens) -> int:
+        """qwen_prefill: n prompt tokens at once (batched tensor-core steps on a BF16 model)."""
+        arr = (c_int * len(tokens))(*[int(t) for t in tokens])
+        return self.L.qwen_prefill(self.handle, arr, len(tokens))
 
     def generate(self, n: int):
         ids = (c_int * n)()

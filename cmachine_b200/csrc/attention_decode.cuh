@@ -127,6 +127,7 @@ constexpr int kSingleClusterRows = 1024;  // caches up to this length use one cl
 
 // Cache rows a CTA stages in shared memory before its dependency wait.
 constexpr int kStagedRows = 80;
+constexpr unsigned kErrStaging = 0x20u;  // fault bit: launched without the staging buffer
 constexpr uint32_t kStagedBytes = 2u * kStagedRows * kHeadDim * sizeof(float);
 
 // Dense FP32 rows [kvheads][capacity][128]; rows 0..position. The rows of a
@@ -424,8 +425,14 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int r0 = min(t1, t0 + warp * per_warp), r1 = min(t1, r0 + per_warp);
     int stage_from = r0;  // rows below this one are staged in shared memory
     if constexpr (Rows::kStaged) {
+        // Stage only into shared memory the launch provided (else load every
+        // row from global memory and record the configuration error).
+        uint32_t dyn;
+        asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        const bool room = dyn >= kStagedBytes;
+        if (!room && tid == 0 && rows.fault) atomicOr(rows.fault, kErrStaging);
         rows.s0 = t0;
-        rows.s1 = max(t0, min(min(t1, rows.prefetch_limit()), t0 + kStagedRows));
+        rows.s1 = room ? max(t0, min(min(t1, rows.prefetch_limit()), t0 + kStagedRows)) : t0;
         rows.ks = reinterpret_cast<const float4 *>(staged);
         rows.vs = reinterpret_cast<const float4 *>(staged + kStagedBytes / 2);
         if (tid == 0) {
@@ -455,7 +462,10 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
     rows.current(lane, warp, cta);
-    if constexpr (Rows::kStaged) mbar_wait(&kv_bar, 0, rows.fault, kErrFullWait);
+    if constexpr (Rows::kStaged) {
+        unsigned lost = 0u;
+        mbar_wait(&kv_bar, 0, rows.fault ? rows.fault : &lost, kErrFullWait);
+    }
 
     float4 q4[G], acc[G];
 #pragma unroll

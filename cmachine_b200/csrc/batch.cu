@@ -709,6 +709,7 @@ struct QwenB200Batch {
     int readout_tiles;
     std::map<int, cudaGraphExec_t> graphs;
     int launches;
+    float *prefill_logits, *prefill_x;  // logits and hidden rows of a prefill chunk's non-final tokens (lazy)
 };
 
 namespace {
@@ -979,7 +980,8 @@ void qwen_b200_batch_free(QwenB200Batch *b) {
     TCM_CUDA(cudaStreamSynchronize(stream()));
     for (auto &g : b->graphs) TCM_CUDA(cudaGraphExecDestroy(g.second));
     void *all[] = {b->st, b->x, b->q, b->nh, b->nl, b->hh, b->hl, b->part, b->counters, b->attn_part,
-                   b->attn_counters, b->top_part, b->log, b->top_counters, b->attn_work};
+                   b->attn_counters, b->top_part, b->log, b->top_counters, b->attn_work, b->prefill_logits,
+                   b->prefill_x};
     for (void *p : all) gpu_free(p);
     TCM_CUDA(cudaFreeHost(b->host));
     TCM_CUDA(cudaFreeHost(b->host_log));
@@ -1134,6 +1136,34 @@ int qwen_b200_batch_step(QwenB200Batch *b, int n, const QwenB200BatchSession *se
     if (!b || !load_sessions(b, n, sessions, tokens, positions)) return -1;
     TCM_CUDA(cudaGraphLaunch(graph_for(b, n), stream()));
     return read_back(b, n, 1, tops);
+}
+
+int qwen_b200_batch_prefill(QwenB200Batch *b, const QwenB200BatchSession *session, const int *tokens, int n,
+                            int position, TcmTop2 *top) {
+    if (!b || !session || !tokens || n < 1 || n > kBN || position < 0 || position + n > session->capacity ||
+        position + n > kAttnSplitMax * kAttnChunk)
+        return -1;
+    if (!b->prefill_logits) {
+        b->prefill_logits = (float *)gpu_alloc((size_t)(kBN - 1) * b->s.vocab * sizeof(float));
+        b->prefill_x = (float *)gpu_alloc((size_t)(kBN - 1) * kHd * sizeof(float));
+    }
+    // Slot i is token i at position + i in the session's own cache: the q/k/v
+    // epilogue appends every slot's row before the attention kernel reads rows
+    // 0..position + i, so the step is causal over the chunk.
+    QwenB200BatchSession ss[kBN];
+    int pos[kBN];
+    TcmTop2 tops[kBN];
+    for (int i = 0; i < n; i++) {
+        ss[i] = *session;
+        if (i < n - 1) {
+            ss[i].logits = b->prefill_logits + (size_t)i * b->s.vocab;
+            ss[i].x = b->prefill_x + (size_t)i * kHd;
+        }
+        pos[i] = position + i;
+    }
+    const int status = qwen_b200_batch_step(b, n, ss, tokens, pos, tops);
+    if (status == 0 && top) *top = tops[n - 1];
+    return status;
 }
 
 int qwen_b200_batch_enqueue(QwenB200Batch *b, int n, const QwenB200BatchSession *sessions, const int *tokens,

@@ -601,6 +601,8 @@ namespace {
 
 void setup_attention() {
     TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6, DenseRows>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6, DenseRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kStagedBytes));
     TCM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<6, ByteRows>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
 }
 template <typename WT> void setup_kernels_typed() {
@@ -658,7 +660,7 @@ void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCluster * kClustersPerHead, s.kvheads);
     cfg.blockDim = dim3(kDecodeAttnThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = Rows::kStaged ? kStagedBytes : 0;
     cfg.stream = stream();
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -678,6 +680,7 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
     rows.values = r->b.values + slot_offset(r, layer);
     rows.capacity = r->b.capacity;
     rows.position = &r->st->position;
+    rows.fault = &r->st->fault;
     launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl);
 }
 void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const float *k, const float *v, float *out,

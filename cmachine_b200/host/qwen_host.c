@@ -435,6 +435,39 @@ done:
     return status;
 }
 
+int qwen_prefill(QwenSession *s, const int *tokens, int n) {
+    if (!s || !tokens || n < 1 || s->phase == 2 || n > s->capacity - s->position) return -1;
+    QwenModel *m = (QwenModel *)s->model;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= m->vocab) return -1;
+    const int batched = m->fused && m->matrix_dtype == 2 && fused_token_ok(s) && !s->observer && !s->cache_guard &&
+                        s->position + n <= 9216;
+    if (batched && !m->batch) m->batch = qwen_b200_batch_create(m->fused);
+    if (!batched || !m->batch) {
+        for (int i = 0; i < n; i++)
+            if (qwen_push(s, tokens[i])) return -1;
+        return 0;
+    }
+    QwenB200BatchSession b = {s->keys, s->values, s->capacity, s->logits, s->x};
+    for (int done = 0; done < n;) {
+        const int c = n - done < qwen_b200_batch_max() ? n - done : qwen_b200_batch_max();
+        TcmTop2 top;
+        int status = qwen_b200_batch_prefill(m->batch, &b, tokens + done, c, s->position, &top);
+        if (status == -3) { fprintf(stderr, "non-finite Qwen logits\n"); exit(2); }
+        if (status) return -1;
+        uint64_t lineage = 0;
+        for (int i = 0; i < c; i++)
+            if (take_id(&next_lineage_id, &lineage)) return -1;
+        snapshot(s, &s->token_parent);
+        s->current_token = tokens[done + c - 1];
+        s->top = top;
+        s->position += c - 1;
+        finish_bookkeeping(s, lineage);
+        done += c;
+    }
+    return 0;
+}
+
 /* ------------------------------------------------------------------ checkpoints */
 
 static int at_boundary(const QwenSession *s) {

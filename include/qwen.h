@@ -157,6 +157,18 @@ int qwen_complete_token(QwenSession *);
  * changed. */
 int qwen_push_batch(QwenSession **sessions, int n, const int *tokens);
 
+/* B200 addition: prefill -- the same session state as n qwen_push calls
+ * (K/V rows, logits, top-2, pending token, position, n lineage ids taken, the
+ * last one kept). For a session qwen_push_batch could serve (BF16 model, fused
+ * decoder, K/V in the session, no observer armed, positions < 9216), the tokens
+ * run as batched tensor-core steps of up to 64 tokens each, every step causal
+ * over its chunk (values within the BF16 profile's tolerance of n pushes);
+ * otherwise it is n qwen_push calls. Returns 0, or -1: refused with the session
+ * unchanged when a token is out of range, the tokens do not fit the capacity or
+ * a token is open; when a cache guard refuses a later token, the tokens before
+ * it stay pushed. */
+int qwen_prefill(QwenSession *, const int *tokens, int n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -164,6 +164,14 @@ int qwen_b200_batch_launches_per_step(const QwenB200Batch *);
  * logits, -4 a pipeline wait ran out. */
 int qwen_b200_batch_step(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
                          const int *positions, TcmTop2 *tops);
+/* Prefill chunk of one session: tokens[0..n) (n <= qwen_b200_batch_max()) at
+ * positions position..position+n-1 as one step whose slots share the session's
+ * cache (causal: every slot's K/V row is appended before any slot attends).
+ * The last token's logits and hidden state go to the session's buffers, its
+ * top-2 to *top; the other tokens' logits go to engine scratch. Returns as
+ * qwen_b200_batch_step. */
+int qwen_b200_batch_prefill(QwenB200Batch *, const QwenB200BatchSession *session, const int *tokens, int n,
+                            int position, TcmTop2 *top);
 /* `steps` chained greedy steps (the device feeds every session's top-1 back and
  * advances its position) without waiting; qwen_b200_batch_read then returns the
  * last step's tops and, if history is set, history[t * n + i] for every step. */

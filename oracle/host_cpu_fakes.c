@@ -98,6 +98,10 @@ void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int writ
 QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) { (void)d; return NULL; }
 void qwen_b200_batch_free(QwenB200Batch *b) { (void)b; }
 int qwen_b200_batch_max(void) { return 64; }
+int qwen_b200_batch_prefill(QwenB200Batch *b, const QwenB200BatchSession *s, const int *t, int n, int p, TcmTop2 *o) {
+    (void)b; (void)s; (void)t; (void)n; (void)p; (void)o;
+    return -1;
+}
 int qwen_b200_batch_step(QwenB200Batch *b, int n, const QwenB200BatchSession *s, const int *t, const int *p, TcmTop2 *o) {
     (void)b; (void)n; (void)s; (void)t; (void)p; (void)o;
     return -1;

@@ -158,3 +158,75 @@ def test_batch_composition_rollback_and_chained_steps():
         for s in crowd:
             s.free()
         model.free()
+
+
+def run_prefill_parity(layers, seed, head, prompt_n, follow, capacity):
+    """Pushes `head` tokens, prefills `prompt_n` (qwen_prefill: batched causal
+    steps of up to 64 tokens), then `follow` greedy pushes; the oracle takes the
+    same tokens one by one."""
+    shape = cm.qwen_shape(layers, 4096)
+    model = cm.Model(shape, seed, cm.TEST_LAW, 2)
+    s = cm.Session(model, capacity)
+    o = CpuDecoder(ORACLE, shape, seed, cm.TEST_LAW, True, capacity)
+    try:
+        for t in tokens(seed * 10, head, shape.vocab):
+            assert s.push(t) == 0
+            o.push(t, readout=False)
+        prompt = tokens(seed * 10 + 1, prompt_n, shape.vocab)
+        latest = s.view().lineage_id
+        assert s.prefill(prompt) == 0
+        for t in prompt[:-1]:
+            o.push(t, readout=False)
+        top, lo = o.push(prompt[-1])
+        v = s.view()
+        assert v.position == head + prompt_n and v.phase == 1
+        assert v.lineage_id - latest == prompt_n
+        worst = float(np.max(np.abs(s.logits() - lo)))
+        if top[2] - top[3] > 2 * BF16_TOL:
+            assert s.pending == top[0]
+        kv = 0.0
+        for layer in range(layers):
+            for kind in (0, 1):
+                kv = max(kv, float(np.max(np.abs(s.kv(layer, kind) - o.kv(layer, kind)))))
+        for _ in range(follow):
+            t = top[0]  # teacher-forced on the oracle's choice
+            assert s.push(t) == 0
+            top, lo = o.push(t)
+            worst = max(worst, float(np.max(np.abs(s.logits() - lo))))
+        return worst, kv
+    finally:
+        o.close()
+        s.free()
+        model.free()
+
+
+def test_prefill_chunks_match_oracle():
+    """75 tokens after 5 pushes: a 64-token chunk and an 11-token chunk."""
+    worst, kv = run_prefill_parity(2, 91, 5, 75, 4, 100)
+    print(f"prefill 2 layers: max|dlogit|={worst:.3e} max|dkv|={kv:.3e}")
+    assert worst <= BF16_TOL and kv <= BF16_TOL
+
+
+def test_prefill_full_depth_matches_oracle():
+    worst, kv = run_prefill_parity(28, 92, 0, 10, 2, 16)
+    print(f"prefill 28 layers: max|dlogit|={worst:.3e} max|dkv|={kv:.3e}")
+    assert worst <= BF16_TOL and kv <= BF16_TOL
+
+
+def test_prefill_of_fp32_model_is_pushes():
+    """The FP32 profile has no batched engine: qwen_prefill is n pushes, bit for bit."""
+    shape = cm.qwen_shape(2, 4096)
+    model = cm.Model(shape, 93, cm.TEST_LAW, 0)
+    a, b = cm.Session(model, 64), cm.Session(model, 64)
+    try:
+        prompt = tokens(930, 20, shape.vocab)
+        assert a.prefill(prompt) == 0
+        for t in prompt:
+            assert b.push(t) == 0
+        assert a.view().position == b.view().position == 20 and a.pending == b.pending
+        assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32))
+        for layer in range(2):
+            for kind in (0, 1):
+                assert np.array_equal(a.kv(layer, kind).view(np.uint32), b.kv(layer, kind).view(np.uint32))
+    finally:
+        a.free(); b.free(); model.free()

@@ -212,3 +212,27 @@ def test_push_batch_refuses_without_the_batched_engine(model):
     assert cm.push_batch([a, b], [1, 2]) == -1
     assert cm.push_batch([a, a], [1, 2]) == -1
     assert bytes(a._buf) == before
+
+
+def test_prefill_equals_pushes_and_refuses_unchanged(model):
+    """qwen_prefill without the batched engine is n qwen_push calls: identical
+    bits and lineage count; refusals (token out of range, capacity, an open
+    token) leave the session unchanged."""
+    a, b = cm.Session(model, 32), cm.Session(model, 32)
+    prefix(a)
+    prefix(b)
+    tokens = [5, 1, 7, 15, 2, 9]
+    latest = b.view().lineage_id  # lineage ids are process-wide: b's prefix took the latest
+    assert a.prefill(tokens) == 0
+    assert a.view().lineage_id - latest == len(tokens)
+    for t in tokens:
+        assert b.push(t) == 0
+    equal(a, b)
+    before = bytes(a._buf)
+    assert a.prefill([1, model.shape.vocab]) == -1
+    assert a.prefill([-1]) == -1
+    assert a.prefill([1] * (32 - a.view().position + 1)) == -1
+    assert bytes(a._buf) == before
+    assert a.begin_token(3) == 0
+    assert a.prefill([1]) == -1
+    a.free(); b.free()
