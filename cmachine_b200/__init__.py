@@ -174,6 +174,7 @@ def _declare(L, strict: bool = True):
         "qwen_b200_session_set_delivered": (None, [P, c_int]),
         "qwen_b200_session_observe": (None, [P, OBSERVER, P, c_int, c_int]),
         "qwen_b200_model_weight_bytes": (c_size_t, [P]), "qwen_b200_model_decoder": (P, [P]),
+        "qwen_b200_model_weight": (P, [P, c_int, c_int]), "qwen_b200_model_matrix_dtype": (c_int, [P]),
         "qwen_b200_session_runner": (P, [P]),
         "qwen_b200_ring_size": (c_size_t, []), "qwen_b200_ring_view": (None, [P, POINTER(RingView)]),
         "qwen_b200_ring_fail": (None, [P, c_int, c_int]),

@@ -14,6 +14,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 LIB = HERE / "libcmachine_b200.so"
+CLI = HERE / "tcm-cuda"
 BUILD = HERE / "_build"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -67,6 +68,16 @@ def build_library(verbose: bool = False) -> Path:
               "-lpthread", "-ldl", "-lrt"])
         if verbose:
             print("link", LIB.name)
+    # The serving executable (the reference's tcm-cuda; tcm-bounded-chat serves a ring).
+    cli = HERE / "cli" / "tcm_cuda.c"
+    if _stale(CLI, [cli, LIB]):
+        _run(["gcc", "-O2", "-std=c11", "-Wall", str(cli), "-o", str(CLI), "-L", str(HERE), "-lcmachine_b200",
+              "-Wl,-rpath,$ORIGIN"])
+        if verbose:
+            print("link", CLI.name)
+    alias = HERE / "tcm-bounded-chat"
+    if not alias.is_symlink():
+        alias.symlink_to(CLI.name)
     return LIB
 
 

@@ -140,6 +140,8 @@ void qwen_b200_register_matrix(const void *p, int rows, int columns, int encoded
     }
 }
 
+int qwen_b200_weight_dtype(const void *p) { return weight_dtype(p) == 2 ? 2 : 1; }
+
 void qwen_b200_unregister_matrix(const void *p) {
     std::lock_guard<std::mutex> hold(g_lock);
     auto it = g_records.find(p);

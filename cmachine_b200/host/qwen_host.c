@@ -103,12 +103,99 @@ int qwen_model_init_seeded(QwenModel *m, const QwenB200Shape *shape, uint64_t se
     return 0;
 }
 
+/* One bundle tensor into device memory (the reference's loader helper,
+ * src/qwen.c:21-24): the name must exist with the given rank and leading
+ * dimensions in FP32 or BF16. */
+static float *bundle_weight(QwenModel *m, const TcmModel *b, const char *name, int rank, int rows, int cols) {
+    const TcmTensor *t = tcm_tensor(b, name);
+    if (!t || t->rank != (uint32_t)rank || t->dim[0] != (uint64_t)rows || (rank == 2 && t->dim[1] != (uint64_t)cols) ||
+        (t->dtype != TCM_F32 && t->dtype != TCM_BF16))
+        return NULL;
+    const size_t count = t->bytes / (t->dtype == TCM_F32 ? 4 : 2);
+    float *p = gpu_owned_weight(m->gpu, t->data, t->dtype, count, rank, rows, cols);
+    m->allocations[m->allocation_count++] = p;
+    m->weight_bytes += gpu_owned_weight_bytes(p, count);
+    return p;
+}
+
+int qwen_model_init(QwenModel *m, const TcmModel *b, char *error, size_t capacity) {
+    memset(m, 0, sizeof(*m));
+    const uint32_t *c = b->config;
+    if (b->architecture != TCM_QWEN || b->count != 338 || c[0] != 1536 || c[1] != 28 || c[2] != 12 || c[3] != 2 ||
+        c[4] != 128 || c[5] != 8960 || c[6] != 151936 || c[10] != 32768) {
+        snprintf(error, capacity, "unsupported Qwen2.5-1.5B profile");
+        return -1;
+    }
+    m->hidden = (int)c[0]; m->layers = (int)c[1]; m->qheads = (int)c[2]; m->kvheads = (int)c[3]; m->head = (int)c[4];
+    m->intermediate = (int)c[5]; m->vocab = (int)c[6]; m->eos = (int)c[9]; m->max_position = (int)c[10];
+    m->eos_extra = (int)c[12];
+    memcpy(&m->epsilon, &c[7], 4);
+    memcpy(&m->theta, &c[8], 4);
+    memcpy(m->identity, b->identity, 65);
+    memcpy(m->digest, b->digest, 65);
+    if (m->epsilon != 1e-6f || m->theta != 1e6f || c[11] != 1) {
+        snprintf(error, capacity, "Qwen numerical configuration differs");
+        memset(m, 0, sizeof(*m));
+        return -1;
+    }
+    m->allocations = calloc(b->count, sizeof(float *));
+    m->layer = calloc((size_t)m->layers, sizeof(QwenLayer));
+    if (!m->allocations || !m->layer) {
+        snprintf(error, capacity, "Qwen descriptor allocation failed");
+        qwen_model_free(m);
+        return -1;
+    }
+    m->gpu = gpu_open();
+    const int d = m->hidden, kv = m->kvheads * m->head, f = m->intermediate;
+    int bad = 0;
+    m->embedding = bundle_weight(m, b, "model.embed_tokens.weight", 2, m->vocab, d);
+    m->norm = bundle_weight(m, b, "model.norm.weight", 1, d, 0);
+    bad |= !m->embedding || !m->norm;
+    for (int i = 0; i < m->layers; i++) {
+        QwenLayer *L = &m->layer[i];
+        struct { float **field; const char *suffix; int rank, rows, cols; } spec[] = {
+            {&L->input_norm, "input_layernorm.weight", 1, d, 0}, {&L->post_norm, "post_attention_layernorm.weight", 1, d, 0},
+            {&L->q, "self_attn.q_proj.weight", 2, d, d}, {&L->k, "self_attn.k_proj.weight", 2, kv, d},
+            {&L->v, "self_attn.v_proj.weight", 2, kv, d}, {&L->qb, "self_attn.q_proj.bias", 1, d, 0},
+            {&L->kb, "self_attn.k_proj.bias", 1, kv, 0}, {&L->vb, "self_attn.v_proj.bias", 1, kv, 0},
+            {&L->o, "self_attn.o_proj.weight", 2, d, d}, {&L->gate, "mlp.gate_proj.weight", 2, f, d},
+            {&L->up, "mlp.up_proj.weight", 2, f, d}, {&L->down, "mlp.down_proj.weight", 2, d, f}};
+        for (size_t j = 0; j < sizeof(spec) / sizeof(spec[0]); j++) {
+            char name[64];
+            snprintf(name, sizeof(name), "model.layers.%d.%s", i, spec[j].suffix);
+            *spec[j].field = bundle_weight(m, b, name, spec[j].rank, spec[j].rows, spec[j].cols);
+            bad |= !*spec[j].field;
+        }
+    }
+    if (bad || m->allocation_count != 338) {
+        snprintf(error, capacity, "Qwen tensor names/shapes differ");
+        qwen_model_free(m);
+        return -1;
+    }
+    /* The fused decoder reads the matrices in their stored type. */
+    QwenB200Shape shape = {m->hidden, m->layers, m->qheads, m->kvheads, m->head, m->intermediate, m->vocab,
+                           m->max_position, m->epsilon, m->theta};
+    QwenB200Layer *layers = calloc((size_t)m->layers, sizeof(QwenB200Layer));
+    if (layers) {
+        for (int l = 0; l < m->layers; l++) {
+            const QwenLayer *L = &m->layer[l];
+            QwenB200Layer one = {L->input_norm, L->post_norm, L->q, L->k, L->v, L->qb, L->kb, L->vb, L->o, L->gate, L->up, L->down};
+            layers[l] = one;
+        }
+        m->fused = qwen_b200_decoder_create(&shape, m->embedding, m->norm, layers, 0);
+        free(layers);
+    }
+    m->matrix_dtype = qwen_b200_weight_dtype(m->embedding);
+    gpu_sync();
+    return 0;
+}
+
 void qwen_model_free(QwenModel *m) {
     if (!m) return;
     qwen_b200_batch_free(m->batch);
     qwen_b200_decoder_free(m->fused);
     for (unsigned i = 0; i < m->allocation_count; i++) {
-        if (m->matrix_dtype == 2) qwen_b200_unregister_matrix(m->allocations[i]);
+        qwen_b200_unregister_matrix(m->allocations[i]);
         gpu_free(m->allocations[i]);
     }
     free(m->allocations);

@@ -56,6 +56,17 @@ void qwen_b200_session_cache_guard(QwenSession *s, QwenCacheGuard guard) { s->ca
 
 size_t qwen_b200_model_weight_bytes(const QwenModel *m) { return m->weight_bytes; }
 const QwenB200Decoder *qwen_b200_model_decoder(const QwenModel *m) { return m->fused; }
+/* Device pointer of a weight: layer -1 kind 0 the embedding, kind 1 the final
+ * norm; layer >= 0 kinds 0..11 input norm, post norm, q, k, v, q bias, k bias,
+ * v bias, o, gate, up, down. NULL when out of range. */
+const void *qwen_b200_model_weight(const QwenModel *m, int layer, int kind) {
+    if (layer == -1) return kind == 0 ? (const void *)m->embedding : kind == 1 ? (const void *)m->norm : NULL;
+    if (layer < 0 || layer >= m->layers || kind < 0 || kind > 11) return NULL;
+    const QwenLayer *L = &m->layer[layer];
+    const float *all[12] = {L->input_norm, L->post_norm, L->q, L->k, L->v, L->qb, L->kb, L->vb, L->o, L->gate, L->up, L->down};
+    return all[kind];
+}
+int qwen_b200_model_matrix_dtype(const QwenModel *m) { return m->matrix_dtype; }
 QwenB200Runner *qwen_b200_session_runner(const QwenSession *s) { return s->runner; }
 
 /* The bounded cache (include/bounded_cache.h), flattened. */

@@ -25,6 +25,7 @@
 #include <stdint.h>
 #include "gpu.h"
 #include "qwen_b200.h"
+#include "tcm_bundle.h"
 #include "tcm_seeded.h"
 #ifdef __cplusplus
 extern "C" {
@@ -112,6 +113,13 @@ typedef struct {
 int qwen_model_init_seeded(QwenModel *, const QwenB200Shape *, uint64_t seed, const TcmFillLaw *law,
                            int weight_profile, int fused);
 void qwen_model_free(QwenModel *);
+/* src/qwen.h:184: a Qwen2.5-1.5B model from a TCM1LE bundle (architecture
+ * TCM_QWEN, 338 tensors, the Qwen2.5-1.5B configuration, epsilon 1e-6, theta
+ * 1e6), the reference's tensor names and shapes, matrices stored per the weight
+ * profile set by gpu_weight_configure (0 FP32, 1 FP32 tiled, 2 source BF16;
+ * vectors FP32). The fused decoder is built over them. 0, or -1 with a message
+ * (the reference's) and *m cleared. */
+int qwen_model_init(QwenModel *, const TcmModel *, char *error, size_t capacity);
 
 /* Sessions and the decode state machine (src/qwen.h:186-204). */
 int qwen_session_init(QwenSession *, const QwenModel *, int capacity);

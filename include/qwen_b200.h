@@ -245,6 +245,8 @@ int qwen_b200_sm_count(void);
  * host upload, so gpu_matvec reads it in its stored type. */
 void qwen_b200_register_matrix(const void *p, int rows, int columns, int encoded);
 void qwen_b200_unregister_matrix(const void *p);
+/* How a device weight is stored: 2 source BF16 (registered encoded), else 1 (FP32). */
+int qwen_b200_weight_dtype(const void *p);
 
 /* Seeded device fill (include/tcm_seeded.h): n values of tensor `id` under
  * model seed `seed` with value offset + N(0,1)*scale, stored as FP32

@@ -98,6 +98,11 @@ void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int writ
 QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) { (void)d; return NULL; }
 void qwen_b200_batch_free(QwenB200Batch *b) { (void)b; }
 int qwen_b200_batch_max(void) { return 64; }
+int qwen_b200_weight_dtype(const void *p) { (void)p; return 1; }
+/* Weight profiles and allocation accounting have no CPU meaning. */
+void gpu_weight_configure(int profile) { (void)profile; }
+void gpu_weight_release(void) {}
+size_t gpu_live_bytes(void) { return 0; }
 int qwen_b200_batch_prefill(QwenB200Batch *b, const QwenB200BatchSession *s, const int *t, int n, int p, TcmTop2 *o) {
     (void)b; (void)s; (void)t; (void)n; (void)p; (void)o;
     return -1;

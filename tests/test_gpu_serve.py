@@ -1,0 +1,128 @@
+"""The serving executable (cmachine_b200/tcm-cuda, the reference's line
+protocol) on the GPU, and TCM1LE bundles end to end:
+
+1. a dense session on a seeded BF16 model: prefill through A, generation,
+   push/rollback and checkpoint/restore restore the state hashes;
+2. a bounded (byte-codec ring) session: marks roll back to identical hashes;
+3. a 28-layer BF16 bundle written from a seeded model's device weights serves
+   exactly as the seeded model itself: same cache and logits hashes after the
+   same commands (qwen_model_init + the source-BF16 weight profile).
+"""
+import ctypes
+import hashlib
+import json
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import cmachine_b200 as cm
+from checkers import ROOT
+
+pytestmark = pytest.mark.gpu
+SERVE = ROOT / "cmachine_b200" / "tcm-cuda"
+
+
+def run(model, commands, *args):
+    proc = subprocess.run([str(SERVE), "serve", model, *args], input="\n".join(commands) + "\n", text=True,
+                          capture_output=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr
+    return [json.loads(line) for line in proc.stdout.splitlines()]
+
+
+def prompt(n, seed=3):
+    return " ".join(str(int(t)) for t in np.random.default_rng(seed).integers(0, 151936, n))
+
+
+def test_dense_session_protocol():
+    out = run("seeded:qwen2.5-1.5b@2:7:2", ["A " + prompt(100), "G 8", "S", "P", "A " + prompt(5, 4), "S", "B 1", "S",
+                                           "C", "G 3", "R", "S", "Q"], "--context", "256")
+    ready, app, gen, s0, pushed, app2, s1, rolled, s2, ck, gen2, restored, s3 = out
+    assert ready["event"] == "ready" and app == {"event": "appended", "count": 100, "position": 100}
+    assert gen["count"] == 8 and gen["position"] == 107
+    assert s0["position"] == 107 and s0["logits_valid"] is True
+    assert app2["position"] == 112 and s1["cache_sha256"] != s0["cache_sha256"]
+    assert rolled["event"] == "rolled_back" and s2["cache_sha256"] == s0["cache_sha256"]
+    assert ck["event"] == "checkpoint" and gen2["count"] == 3
+    assert restored["position"] == 107 and s3["cache_sha256"] == s0["cache_sha256"]
+
+
+def test_bounded_session_protocol():
+    out = run("seeded:qwen2.5-1.5b:7:2", ["A " + prompt(60), "G 4", "S", "P", "A " + prompt(20, 5), "S", "B 1", "S",
+                                         "Q"], "--cache-policy", "bounded", "--context", "256", "--anchors", "8",
+              "--recent", "32", "--reservoir", "16")
+    ready, app, gen, s0, pushed, app2, s1, rolled, s2 = out
+    assert ready["cache_policy"] == "bounded" and ready["resident_capacity"] == 56
+    assert app["position"] == 60 and gen["count"] == 4
+    assert s0["resident_rows"] == 56 and s0["evictions"] > 0
+    assert s1["cache_sha256"] != s0["cache_sha256"]
+    assert rolled["event"] == "rolled_back" and s2["cache_sha256"] == s0["cache_sha256"]
+    assert s2["logits_sha256"] == s0["logits_sha256"]
+
+
+def write_model_bundle(path, model):
+    """A TCM1LE bundle (the reference's tensor names, BF16 matrices, FP32
+    vectors) holding a seeded model's device weights."""
+    L, s = model.L, model.shape
+    d, kv, f = s.hidden, s.kvheads * s.head, s.intermediate
+    specs = [("model.embed_tokens.weight", -1, 0, (s.vocab, d)), ("model.norm.weight", -1, 1, (d,))]
+    suffix = ["input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+              "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.q_proj.bias", "self_attn.k_proj.bias",
+              "self_attn.v_proj.bias", "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
+              "mlp.down_proj.weight"]
+    shapes = [(d,), (d,), (d, d), (kv, d), (kv, d), (d,), (kv,), (kv,), (d, d), (f, d), (f, d), (d, f)]
+    for layer in range(s.layers):
+        for kind in range(12):
+            specs.append((f"model.layers.{layer}.{suffix[kind]}", layer, kind, shapes[kind]))
+    specs.sort(key=lambda x: x[0])
+    offset = 176 + 120 * len(specs)
+    records, layout = [], []
+    for name, layer, kind, shape in specs:
+        dtype = 2 if len(shape) == 2 else 1
+        nbytes = int(np.prod(shape)) * (2 if dtype == 2 else 4)
+        offset += (-offset) % 8
+        records.append(struct.pack("<64sII4QQQ", name.encode(), len(shape), dtype, *(list(shape) + [0] * (4 - len(shape))),
+                                   offset, nbytes))
+        layout.append((offset, layer, kind, nbytes))
+        offset += nbytes
+    config = [1536, 28, 12, 2, 128, 8960, 151936, struct.unpack("<I", struct.pack("<f", 1e-6))[0],
+              struct.unpack("<I", struct.pack("<f", 1e6))[0], 151935, 32768, 1, 0]
+    head = struct.pack("<II16I64s", 2, len(specs), *(config + [0] * 3), hashlib.sha256(b"seeded").hexdigest().encode())
+    digest = hashlib.sha256()
+    with open(path, "wb") as out:
+        out.write(b"TCM1LE\0\0" + bytes(32))
+        for block in (head, b"".join(records)):
+            out.write(block)
+            digest.update(block)
+        pos = 176 + 120 * len(specs)
+        for off, layer, kind, nbytes in layout:
+            pad = bytes(off - pos)
+            host = np.empty(nbytes, np.uint8)
+            L.gpu_read(cm.ptr(host), ctypes.c_void_p(L.qwen_b200_model_weight(model.handle, layer, kind)), nbytes)
+            for block in (pad, host.tobytes()):
+                out.write(block)
+                digest.update(block)
+            pos = off + nbytes
+        out.seek(8)
+        out.write(digest.digest())
+
+
+def test_bundle_serves_as_the_seeded_model(tmp_path):
+    seed = 11
+    model = cm.Model(cm.qwen_shape(28, 32768), seed, cm.BENCH_LAW, 2)
+    assert model.L.qwen_b200_model_matrix_dtype(model.handle) == 2
+    path = tmp_path / "qwen.tcm"
+    write_model_bundle(path, model)
+    model.free()
+    script = ["A " + prompt(40), "S", "G 3", "S", "P", "A 5 6 7", "B 1", "S", "Q"]
+    args = ["--cache-policy", "bounded", "--context", "128", "--anchors", "4", "--recent", "16", "--reservoir", "8"]
+    from_bundle = run(str(path), script, *args)
+    seeded = run(f"seeded:qwen2.5-1.5b:{seed}:2", script, *args)
+    assert from_bundle[0]["model_digest"] == hashlib.sha256(path.read_bytes()[40:]).hexdigest()
+    assert from_bundle[0]["weight_profile"] == 2 and from_bundle[0]["gpu_weight_bytes"] == seeded[0]["gpu_weight_bytes"]
+    for a, b in zip(from_bundle[1:], seeded[1:]):
+        if a.get("event") == "state":
+            assert a["cache_sha256"] == b["cache_sha256"] and a["logits_sha256"] == b["logits_sha256"]
+        else:
+            assert a == b
