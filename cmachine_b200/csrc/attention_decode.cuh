@@ -390,7 +390,7 @@ __device__ __forceinline__ void flash_rows(const Rows &rows, int r0, int r1, con
 template <int G, class Rows>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     Rows rows, const float *__restrict__ q, float inv_sqrt_dim, float *__restrict__ part,
-    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace) {
+    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace, int defer) {
     static_assert(G <= 8, "query heads per KV head are padded to eight");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
@@ -461,16 +461,25 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     pdl_wait();
     if (mark && tid == 0) mark[1] = attn_clock();
     pdl_trigger();
+    // This KV head's G query rows, read once per CTA (every warp needs all of
+    // them) and passed on through shared memory: the warps' accumulator
+    // buffer, which is not written before cta_merge's first barrier.
+    static_assert(G * kHeadDim / 4 <= kDecodeAttnThreads, "one 16-byte piece of q per thread");
+    float4 qpiece = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < G * kHeadDim / 4) qpiece = __ldcg(reinterpret_cast<const float4 *>(q + (size_t)kvh * G * kHeadDim) + tid);
     rows.current(lane, warp, cta);
     if constexpr (Rows::kStaged) {
         unsigned lost = 0u;
         mbar_wait(&kv_bar, 0, rows.fault ? rows.fault : &lost, kErrFullWait);
     }
+    float *q_s = &wacc[0][0][0];
+    if (tid < G * kHeadDim / 4) reinterpret_cast<float4 *>(q_s)[tid] = qpiece;
+    __syncthreads();
 
     float4 q4[G], acc[G];
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        q4[g] = reinterpret_cast<const float4 *>(q + ((size_t)kvh * G + g) * kHeadDim)[lane];
+        q4[g] = reinterpret_cast<const float4 *>(q_s + g * kHeadDim)[lane];
         acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float m[G], l[G];
@@ -482,7 +491,10 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     cluster.sync();
     constexpr int kOutPer = G * kHeadDim / kCluster;
     static_assert(G * kHeadDim % kCluster == 0 && kOutPer <= kDecodeAttnThreads, "cluster output split");
-    float *cpart = multi ? part + ((size_t)kvh * clusters + cid) * kAttnPartialFloats : nullptr;
+    // Deferred (defer != 0): every used cluster leaves its partial in `part`
+    // and the next launch folds them (unused clusters' partials are marked
+    // empty); `out` and `counters` are not touched.
+    float *cpart = multi || defer ? part + ((size_t)kvh * clusters + cid) * kAttnPartialFloats : nullptr;
     if (tid < kOutPer) {
         const int o = rank * kOutPer + tid, g = o / kHeadDim, d = o % kHeadDim;
         float mr[kCluster], lr[kCluster], ar[kCluster];
@@ -504,7 +516,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
             den = fmaf(e, lr[r], den);
             num = fmaf(e, ar[r], num);
         }
-        if (!multi) {
+        if (!cpart) {
             out[((size_t)kvh * G + g) * kHeadDim + d] = __fdiv_rn(num, den);
         } else {
             cpart[2 * kAttnMaxGroup + g * kHeadDim + d] = num;
@@ -512,8 +524,12 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
             cpart[kAttnMaxGroup + g] = den;
         }
     }
+    if (defer && !multi && rank == 0 && tid < (clusters - 1) * kAttnMaxGroup) {
+        const int c = 1 + tid / kAttnMaxGroup, g = tid % kAttnMaxGroup;
+        part[((size_t)kvh * clusters + c) * kAttnPartialFloats + g] = -INFINITY;
+    }
     cluster.sync();  // no CTA leaves while another still reads its partial
-    if (multi) {
+    if (multi && !defer) {
         // The last CTA of the head to arrive merges the clusters' partials.
         __threadfence();
         __syncthreads();

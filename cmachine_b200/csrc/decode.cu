@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
     __shared__ float res[2][R];
     __shared__ float bias_s[2 * kMaxPairsPerCta];
     __shared__ float den_s[kHeadDim / 2];
-    __shared__ __align__(16) float nw_s[kHidden];
+    __shared__ __align__(16) float nw_s[kHidden], x_s[kHidden];
     __shared__ int fail_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pairs = (a.qheads + 2 * a.kvheads) * 64;
@@ -95,9 +95,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
         load_lane_row<WT>(xr, (const WT *)a.embed + (size_t)a.st->token * kHidden, lane);
         if (blockIdx.x == 0 && warp == 0) store_lane_vec<WT>(a.x, xr, lane);
     } else {
-        load_lane_vec<WT>(xr, a.x, lane);
+        copy_hidden(x_s, a.x);
     }
     consumers_sync();
+    if (!a.embed) load_lane_vec<WT>(xr, x_s, lane);
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     trace_mark(a.trace, 2);
     const int groups = (items + R - 1) / R;
@@ -150,15 +151,83 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
 // ---------------------------------------------------------------- stage 3: O projection + residual
 struct ORowsArgs {
     const void *w;
-    const float *in;
+    float *in;           // the attention output (written here when `part` is set)
+    const float *part;   // the attention's cluster partials to fold first, or null
     float *x;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
+    int group;           // query heads per KV head
 };
+// The deferred end of attn_decode_kernel: outputs o = threadIdx.x + 256 k
+// (head o / 128, dimension o % 128) into v_s, each from the kClustersPerHead
+// cluster partials (M, den, num) of its KV head, folded exactly as the
+// kernel's own last CTA would fold them; a head with one non-empty partial
+// gives num / den directly, as the one-cluster kernel does. M and den of every
+// (KV head, cluster) are read once per CTA into ml_s (every thread needs them:
+// read per thread, their few lines would take thousands of requests each),
+// while each thread's num loads are in flight. Contains two consumers_syncs.
+constexpr int kFoldHeads = kHidden / kHeadDim;  // query heads of the fused geometry
+__device__ __forceinline__ void fold_attention(float *v_s, float (*ml_s)[kClustersPerHead][2 * kAttnMaxGroup],
+                                               const float *__restrict__ part, int group) {
+    constexpr int kPer = kHidden / (kConsumerWarps * 32);  // 6 outputs per thread
+    constexpr int C = kClustersPerHead;
+    const int nml = kFoldHeads / group * C * 2 * kAttnMaxGroup;
+    for (int i = threadIdx.x; i < nml; i += kConsumerWarps * 32) {
+        const int kc = i / (2 * kAttnMaxGroup), j = i % (2 * kAttnMaxGroup);
+        ml_s[kc / C][kc % C][j] = __ldcg(part + (size_t)kc * kAttnPartialFloats + j);
+    }
+    float ac[kPer][C];
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+        const int o = threadIdx.x + kConsumerWarps * 32 * k;
+        const int head = o / kHeadDim, kvh = head / group, g = head % group, d = o % kHeadDim;
+        const float *hp = part + (size_t)kvh * C * kAttnPartialFloats + 2 * kAttnMaxGroup + g * kHeadDim + d;
+#pragma unroll
+        for (int c = 0; c < C; c++) ac[k][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats);
+    }
+    consumers_sync();
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+        const int o = threadIdx.x + kConsumerWarps * 32 * k;
+        const int head = o / kHeadDim, kvh = head / group, g = head % group;
+        float mc[C], lc[C];
+#pragma unroll
+        for (int c = 0; c < C; c++) {
+            mc[c] = ml_s[kvh][c][g];
+            lc[c] = ml_s[kvh][c][kAttnMaxGroup + g];
+        }
+        int valid = 0;
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; c++)
+            if (mc[c] != -INFINITY) {
+                valid++;
+                num = ac[k][c];
+                den = lc[c];
+            }
+        if (valid > 1) {
+            float M = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < C; c++) M = fmaxf(M, mc[c]);
+            num = 0.f;
+            den = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; c++) {
+                if (mc[c] == -INFINITY) continue;
+                const float e = expf(mc[c] - M);
+                den = fmaf(e, lc[c], den);
+                num = fmaf(e, ac[k][c], num);
+            }
+        }
+        v_s[o] = __fdiv_rn(num, den);
+    }
+}
 template <typename WT>
 __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int R = Geo<WT>::R;
+    __shared__ __align__(16) float in_s[kHidden];
+    __shared__ float ml_s[kFoldHeads][kClustersPerHead][2 * kAttnMaxGroup];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = share_begin(kHidden, blockIdx.x, gridDim.x), r1 = share_begin(kHidden, blockIdx.x + 1, gridDim.x);
     const int items = r1 - r0;
@@ -174,8 +243,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
     }
     pdl_wait();
     trace_mark(a.trace, 1);
+    if (a.part) fold_attention(in_s, ml_s, a.part, a.group);
+    else copy_hidden(in_s, a.in);
+    consumers_sync();
     float xr[kLaneX];
-    load_lane_vec<WT>(xr, a.in, lane);
+    load_lane_vec<WT>(xr, in_s, lane);
+    if (a.part && blockIdx.x == 0)  // the attention output, for readers after this launch
+        for (int i = threadIdx.x; i < kHidden / 4; i += kConsumerWarps * 32)
+            reinterpret_cast<float4 *>(a.in)[i] = reinterpret_cast<const float4 *>(in_s)[i];
     trace_mark(a.trace, 2);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
@@ -212,7 +287,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int R = Geo<WT>::R;
     __shared__ float res[2][R];
-    __shared__ __align__(16) float nw_s[kHidden];
+    __shared__ __align__(16) float nw_s[kHidden], x_s[kHidden];
     __shared__ int fail_s, hdr_s[kStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = 2 * kInter;
@@ -232,8 +307,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     pdl_wait();
     trace_mark(a.trace, 1);
     float xr[kLaneX];
-    load_lane_vec<WT>(xr, a.x, lane);
+    copy_hidden(x_s, a.x);
     consumers_sync();
+    load_lane_vec<WT>(xr, x_s, lane);
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     trace_mark(a.trace, 2);
     for (int g = 0;; g++) {
@@ -365,7 +441,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     constexpr int R = Geo<WT>::R;
     __shared__ float sv[2 * kConsumerWarps];
     __shared__ int si[2 * kConsumerWarps];
-    __shared__ __align__(16) float nw_s[kHidden];
+    __shared__ __align__(16) float nw_s[kHidden], x_s[kHidden];
     __shared__ int last, hdr_s[kStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = a.vocab;
@@ -383,8 +459,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     pdl_wait();
     trace_mark(a.trace, 1);
     float xr[kLaneX];
-    load_lane_vec<WT>(xr, a.x, lane);
+    copy_hidden(x_s, a.x);
     consumers_sync();
+    load_lane_vec<WT>(xr, x_s, lane);
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     Top2 t = top2_empty();
     bool bad = false;
@@ -654,8 +731,10 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.trace = trace_slot(r);
     launch(qkv_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
 }
+// defer: leave the cluster partials in attn_part for the O projection to fold
+// (out is then written by that launch).
 template <class Rows>
-void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl) {
+void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl, bool defer) {
     const QwenB200Shape &s = r->d->s;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCluster * kClustersPerHead, s.kvheads);
@@ -672,19 +751,20 @@ void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, 
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
     TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6, Rows>, rows, q, 1.0f / sqrtf((float)kHeadDim),
-                                r->attn_part, r->attn_counters, out, trace_slot(r)));
+                                r->attn_part, r->attn_counters, out, trace_slot(r),
+                                defer ? 1 : 0));
 }
-void launch_attention(QwenB200Runner *r, int layer, bool pdl) {
+void launch_attention(QwenB200Runner *r, int layer, bool pdl, bool defer = false) {
     DenseRows rows = {};
     rows.keys = r->b.keys + slot_offset(r, layer);
     rows.values = r->b.values + slot_offset(r, layer);
     rows.capacity = r->b.capacity;
     rows.position = &r->st->position;
     rows.fault = &r->st->fault;
-    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl);
+    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl, defer);
 }
 void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const float *k, const float *v, float *out,
-                           bool pdl) {
+                           bool pdl, bool defer = false) {
     const QwenB200Ring &g = r->ring;
     ByteRows rows = {};
     rows.arena = (const signed char *)g.arena + (size_t)layer * g.rows * kRingRowBytes;
@@ -695,7 +775,7 @@ void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const f
     rows.kcur = k;
     rows.vcur = v;
     rows.invalid = &r->st->invalid;
-    launch_attention_rows(r, rows, q, out, pdl);
+    launch_attention_rows(r, rows, q, out, pdl, defer);
 }
 void launch_ring_cut(QwenB200Runner *r, const DecodeState *st, int write_slot, int sample_slot, int mode, bool logits,
                      bool pdl) {
@@ -704,8 +784,11 @@ void launch_ring_cut(QwenB200Runner *r, const DecodeState *st, int write_slot, i
                      st, g.rows, r->d->s.layers, r->d->s.vocab, write_slot, sample_slot, mode};
     launch(ring_cut_kernel, dim3(r->grid), dim3(256), 0, stream(), pdl, a);
 }
-template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl) {
-    ORowsArgs o = {r->d->layers[layer].o, r->b.attention, r->b.x, r->st, trace_slot(r)};
+// fold: the attention launch before this one deferred its cluster fold.
+template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl, bool fold = false) {
+    const QwenB200Shape &s = r->d->s;
+    ORowsArgs o = {r->d->layers[layer].o, r->b.attention, fold ? r->attn_part : nullptr, r->b.x, r->st, trace_slot(r),
+                   s.qheads / s.kvheads};
     launch(oproj_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
 }
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
@@ -719,8 +802,8 @@ template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) 
     launch(down_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kDownStages, kDownStage<WT>), stream(),
            pdl, dn);
 }
-template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl) {
-    launch_oproj<WT>(r, layer, pdl);
+template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl, bool fold = false) {
+    launch_oproj<WT>(r, layer, pdl, fold);
     launch_gateup<WT>(r, layer, true);
     launch_down<WT>(r, layer, true);
 }
@@ -735,10 +818,12 @@ template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
 void launch_layer(QwenB200Runner *r, int layer, bool pdl_first) {
     if (r->d->dtype == 2) launch_qkv<uint16_t>(r, layer, pdl_first);
     else launch_qkv<float>(r, layer, pdl_first);
-    if (has_dense(r, layer)) launch_attention(r, layer, true);
-    else launch_ring_attention(r, layer, r->b.q, r->b.k, r->b.v, r->b.attention, true);
-    if (r->d->dtype == 2) launch_mlp<uint16_t>(r, layer, true);
-    else launch_mlp<float>(r, layer, true);
+    // The O projection folds the attention's cluster partials (one dependent
+    // step less than folding them in the attention's last CTA).
+    if (has_dense(r, layer)) launch_attention(r, layer, true, true);
+    else launch_ring_attention(r, layer, r->b.q, r->b.k, r->b.v, r->b.attention, true, true);
+    if (r->d->dtype == 2) launch_mlp<uint16_t>(r, layer, true, true);
+    else launch_mlp<float>(r, layer, true, true);
 }
 void launch_finish(QwenB200Runner *r, bool pdl) {
     if (r->d->dtype == 2) launch_readout<uint16_t>(r, pdl);

@@ -62,6 +62,15 @@ __device__ __forceinline__ void load_lane_vec(float (&xr)[kLaneX], const float *
             xr[E * k + 4 * h + 3] = f.w;
         }
 }
+// A 1536-float vector from global memory into shared memory by the consumer
+// threads, 16 bytes each per pass; the caller's next consumers_sync publishes
+// it. Every warp of every CTA needs the whole vector: read per warp, each of
+// its 48 lines would take 8 x 148 requests at one L2 slice right after the
+// dependency wait; staged, it takes one per CTA.
+__device__ __forceinline__ void copy_hidden(float *v_s, const float *v) {
+    for (int i = threadIdx.x; i < kHidden / 4; i += kConsumerWarps * 32)
+        reinterpret_cast<float4 *>(v_s)[i] = __ldcg(reinterpret_cast<const float4 *>(v) + i);
+}
 template <typename WT> __device__ __forceinline__ void store_lane_vec(float *x, const float (&xr)[kLaneX], int lane) {
     constexpr int E = Geo<WT>::E;
 #pragma unroll

@@ -62,10 +62,11 @@ def main():
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--mode", choices=["graph", "persistent"], default="persistent")
     ap.add_argument("--lookahead", type=int, default=-1, help="persistent kernel L2 prefetch distance (KB)")
+    ap.add_argument("--time", type=int, default=0, help="then time this many chained greedy tokens (device time)")
     args = ap.parse_args()
     L = cm.lib()
     model = cm.Model(cm.qwen_shape(args.layers, 32768), 2026, cm.BENCH_LAW, args.profile)
-    s = cm.Session(model, args.prompt + args.tokens + 1)
+    s = cm.Session(model, args.prompt + args.tokens + 9 + args.time)
     for i in range(args.prompt):
         assert s.push((i * 7919 + 11) % model.shape.vocab) == 0
     runner = s.runner
@@ -121,6 +122,18 @@ def main():
                  for k in ("release_spread", "cta_ready", "cta_work", "done_spread", "lead")]
         print(f"{kind:10s} {b:9.2f} {rr:10.2f} {rd:11.2f} {sp:8.2f} {extra[0]:10.2f} {extra[1]:9.2f} {extra[2]:9.2f}"
               f" {extra[3]:11.2f} {extra[4]:8.2f}")
+    if args.time:
+        # Chained greedy tokens from the same position, twice (device time between marks 0 and 1).
+        pos0 = args.prompt + args.tokens
+        for rep in range(2):
+            assert L.qwen_b200_enqueue(runner, 1, pos0, 8) == 0
+            L.gpu_sync()
+            L.qwen_b200_mark(0)
+            assert L.qwen_b200_enqueue(runner, 1, pos0, args.time) == 0
+            L.qwen_b200_mark(1)
+            L.gpu_sync()
+            ms = L.qwen_b200_elapsed_ms(0, 1) / args.time
+            print(f"{ms * 1000:.1f} us/token ({1000 / ms:.1f} tokens/s) over {args.time} chained tokens")
     s.free()
     model.free()
 
