@@ -353,6 +353,17 @@ __device__ __forceinline__ void flash_step3(const float4 (&q4)[3], const float4 
     }
 }
 
+// The first cache row of session n that this step's q/k/v GEMM writes: its
+// position, or, when several slots share its cache (a prefill chunk at
+// consecutive positions), the smallest of their positions. Copies of rows at or
+// above it wait for the GEMM.
+__device__ __forceinline__ int first_fresh_row(const BatchState *st, int n_active, int n) {
+    int fresh = st->position[n];
+    for (int m = 0; m < n_active; m++)
+        if (st->keys[m] == st->keys[n]) fresh = min(fresh, st->position[m]);
+    return fresh;
+}
+
 // 16 consumer warps: warp w takes rows 4 (w / 2) .. + 3 of each 32-row stage for
 // query heads 3 (w % 2) .. + 2 of the KV head; one producer warp.
 constexpr int kBatchAttnWarps = 16;
@@ -363,6 +374,7 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
     constexpr int G = 6, GH = 3;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int chunk_start[kBN + 1];   // first item of each session (prefix over sessions)
+    __shared__ int fresh_s[kBN];           // first cache row of each session this step writes
     __shared__ int stage_item[kAttnRingStages], stage_row[kAttnRingStages];
     __shared__ float wm[kBatchAttnWarps][GH], wl[kBatchAttnWarps][GH];
     __shared__ __align__(16) float wacc[kBatchAttnWarps][GH][kHeadDim];
@@ -394,6 +406,7 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
         }
         chunk_start[n_active] = acc_items;
     }
+    if ((int)threadIdx.x < n_active) fresh_s[threadIdx.x] = first_fresh_row(a.st, n_active, threadIdx.x);
     __syncthreads();
     const int items = chunk_start[n_active];
     auto locate = [&](int item, int &n, int &h, int &c, int &rows0, int &rows1) {
@@ -424,7 +437,7 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
                 const bool done = item >= items;
                 int n = 0, h = 0, c = 0, r0 = 0, r1 = 1;
                 if (!done) locate(item, n, h, c, r0, r1);
-                const int cap = done ? 0 : a.st->capacity[n], last = done ? 0 : a.st->position[n];
+                const int cap = done ? 0 : a.st->capacity[n], last = done ? 0 : fresh_s[n];
                 const float *kb = done ? nullptr : a.st->keys[n] + ((size_t)a.layer * 2 + h) * cap * kHeadDim;
                 const float *vb = done ? nullptr : a.st->values[n] + ((size_t)a.layer * 2 + h) * cap * kHeadDim;
                 for (int t = r0; t < r1; t += kAttnRowsPerStage, g++) {
@@ -441,7 +454,7 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
                         g++;  // counted, so the drain below sees each stage's latest phase
                         break;
                     }
-                    if (!waited && t + rows > last) {  // this stage holds the newest row
+                    if (!waited && t + rows > last) {  // this stage holds a row the q/k/v GEMM writes
                         pdl_wait();
                         waited = true;
                     }
@@ -569,6 +582,368 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
             a.work[0] = 0u;
             a.work[1] = 0u;
         }
+    }
+}
+
+// ---------------------------------------------------------------- attention on tensor-core fragments
+// The same work items, with the arithmetic on the tensor cores (mma.sync
+// m16n8k8, TF32 operands, FP32 accumulation) and no sharing between warps:
+// each of the CTA's four warps takes whole items from the global counter and
+// feeds itself through its own three stages of 16 K rows and 16 V rows (each
+// lane moves 16-byte pieces with cp.async; K rows land 576 bytes apart and V
+// rows 528, so every fragment load below is free of bank conflicts; a stage's
+// barrier completes when all 32 lanes' pieces have landed), issuing the next
+// stage's copies as soon as it has read a stage. A warp never waits for
+// another.
+//
+// Per stage and KV head (6 query heads, padded to 8):
+//   S = Q K^T: A = [Q_hi; Q_lo] (rows 0-7 the heads' high TF32 parts, rows
+//     8-15 the remainders), B = K_hi^T and then K_lo^T, so two products give
+//     all four terms of (Q_hi + Q_lo)(K_hi + K_lo); the dimension order inside
+//     each k-step of 8 is permuted (lane slot t <-> dimension 4t, slot t + 4
+//     <-> 4t + 1 of a 16-dimension block), identically for A and B;
+//   online softmax in base 2 on the accumulator layout: lane (g, t) holds
+//     head g's scores of rows 2t and 2t + 1 of each 8-row tile;
+//   O += P V: A = [P_hi; P_lo] straight from those registers (row slot t <->
+//     row 2t, slot t + 4 <-> 2t + 1), B = V_hi and then V_lo.
+// x_hi keeps the TF32 bits of x and x_lo = x - x_hi (exact), so every product
+// carries about 21 bits of each operand: FP32-level scores and outputs.
+// Each item leaves a partial (max, sum, accumulators) in global memory, and
+// batch_attn_merge_kernel folds a (session, head)'s partials in chunk order.
+constexpr int kTcWarps = 4;
+constexpr int kTcRows = 16;                // cache rows per stage
+constexpr int kTcStages = 3;               // stages per warp
+constexpr int kTcKStride = kHeadDim + 16;  // K row stride in floats (576 bytes)
+constexpr int kTcVStride = kHeadDim + 4;   // V row stride in floats (528 bytes)
+constexpr uint32_t kTcStageBytes = (uint32_t)kTcRows * (kTcKStride + kTcVStride) * 4;
+constexpr size_t kTcAttnSmem = (size_t)kTcWarps * kTcStages * kTcStageBytes + (size_t)kTcWarps * kTcStages * 8;
+constexpr int kTcItemRowsDefault = 256;
+static_assert(kTcAttnSmem <= 227 * 1024, "shared memory");
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// 16-byte global -> shared copy (L2 only), and an arrival on `bar` once all of
+// this thread's earlier copies have landed (counted in the barrier's arrival
+// count, which this does not raise).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ uint32_t tf32_hi(float x) { return __float_as_uint(x) & 0xffffe000u; }
+__device__ __forceinline__ uint32_t tf32_lo(float x) { return __float_as_uint(__fsub_rn(x, __uint_as_float(tf32_hi(x)))); }
+
+// O += [P_hi; P_lo] V over one 8-row k-step: v0 and v1 point at this lane's
+// rows 2t and 2t + 1 (already offset by 4g dimensions); masked rows read 0.
+template <bool kMask>
+__device__ __forceinline__ void tc_pv_step(float (&o)[16][4], const uint32_t (&pa)[4], const float *v0, const float *v1,
+                                           bool ok0, bool ok1) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        float4 y = *reinterpret_cast<const float4 *>(v0 + 32 * q), z = *reinterpret_cast<const float4 *>(v1 + 32 * q);
+        if constexpr (kMask) {
+            if (!ok0) y = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (!ok1) z = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const float yy[4] = {y.x, y.y, y.z, y.w}, zz[4] = {z.x, z.y, z.z, z.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            mma_tf32(o[4 * q + i], pa, tf32_hi(yy[i]), tf32_hi(zz[i]));
+            mma_tf32(o[4 * q + i], pa, tf32_lo(yy[i]), tf32_lo(zz[i]));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kTcWarps * 32, 1) batch_attn_tc_kernel(AttnArgs a) {
+    constexpr int G = 6;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int chunk_start[kBN + 1], fresh_s[kBN];
+    __shared__ int hdr_item[kTcWarps][kTcStages], hdr_row[kTcWarps][kTcStages];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    unsigned char *ring = smem + (size_t)warp * kTcStages * kTcStageBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)kTcWarps * kTcStages * kTcStageBytes) + warp * kTcStages;
+    if (lane == 0) {
+        for (int st = 0; st < kTcStages; st++) mbar_init(&full[st], 32);  // one arrival per lane
+        mbar_fence_init();
+    }
+    pdl_trigger();
+    if (threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 0] = global_ns();
+    const int n_active = a.st->n;
+    if (threadIdx.x == 0) {
+        int acc_items = 0;
+        for (int n = 0; n < n_active; n++) {
+            chunk_start[n] = acc_items;
+            acc_items += 2 * ((a.st->position[n] + a.item_rows) / a.item_rows);
+        }
+        chunk_start[n_active] = acc_items;
+    }
+    if ((int)threadIdx.x < n_active) fresh_s[threadIdx.x] = first_fresh_row(a.st, n_active, threadIdx.x);
+    __syncthreads();
+    const int items = chunk_start[n_active];
+    auto locate = [&](int item, int &n, int &h, int &c, int &rows0, int &rows1) {
+        int lo = 0, hi = n_active - 1;  // last session with chunk_start <= item
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (chunk_start[mid] <= item) lo = mid;
+            else hi = mid - 1;
+        }
+        n = lo;
+        const int within = item - chunk_start[n], chunks = (chunk_start[n + 1] - chunk_start[n]) / 2;
+        h = within / chunks;
+        c = within % chunks;
+        rows0 = c * a.item_rows;
+        rows1 = min(a.st->position[n] + 1, rows0 + a.item_rows);
+    };
+
+    // Producer side (warp-uniform state): the item being copied and its next row.
+    int p_item = 0, p_n = 0, p_h = 0, p_c = 0, p_t = 0, p_r1 = 0, produced = 0;
+    bool p_end = false, end_issued = false, waited = false;
+    auto next_item = [&]() {
+        int it = 0;
+        if (lane == 0) it = (int)atomicAdd(&a.work[0], 1u);
+        it = __shfl_sync(0xffffffffu, it, 0);
+        if (it >= items) {
+            p_end = true;
+            return;
+        }
+        p_item = it;
+        locate(it, p_n, p_h, p_c, p_t, p_r1);
+    };
+    auto produce = [&]() {
+        if (end_issued) return;
+        const int s = produced % kTcStages;
+        produced++;
+        if (p_end) {
+            end_issued = true;
+            if (lane == 0) hdr_item[warp][s] = -1;
+            __syncwarp();
+            mbar_arrive(&full[s]);  // the end marker: no data
+            return;
+        }
+        const int rows = min(kTcRows, p_r1 - p_t);
+        if (!waited && p_t + rows > fresh_s[p_n]) {  // rows the q/k/v GEMM writes this step
+            pdl_wait();
+            waited = true;
+        }
+        if (lane == 0) {
+            hdr_item[warp][s] = p_item;
+            hdr_row[warp][s] = p_t;
+        }
+        __syncwarp();
+        const size_t base = (((size_t)a.layer * 2 + p_h) * a.st->capacity[p_n] + p_t) * kHeadDim + 4 * lane;
+        const float *kg = a.st->keys[p_n] + base, *vg = a.st->values[p_n] + base;
+        float *kd = reinterpret_cast<float *>(ring + (size_t)s * kTcStageBytes) + 4 * lane;
+        float *vd = kd + kTcRows * kTcKStride;
+        for (int r = 0; r < rows; r++) {
+            cp_async16(kd + r * kTcKStride, kg + (size_t)r * kHeadDim);
+            cp_async16(vd + r * kTcVStride, vg + (size_t)r * kHeadDim);
+        }
+        cp_async_arrive(&full[s]);
+        p_t += rows;
+        if (p_t >= p_r1) next_item();
+    };
+    next_item();
+    for (int k = 0; k < kTcStages; k++) produce();
+    if (!waited) {  // q is the q/k/v GEMM's output
+        pdl_wait();
+        waited = true;
+    }
+    if (threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 1] = global_ns();
+
+    const float scale2 = a.inv_sqrt_dim * 1.44269504088896340736f;  // log2(e) / sqrt(128): base-2 scores
+    uint32_t qa[16][4];
+    float o[16][4];
+    float m_run = -INFINITY, l_run = 0.f;
+    int cur = -1, cn = 0, ch = 0, cc = 0, cr1 = 0;
+    auto finish = [&]() {
+        float lt = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+        float *pc = a.part + (((size_t)cn * 2 + ch) * kAttnItemMax + cc) * kAttnPartialFloats;
+        if (g < G) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                float *dst = pc + 2 * kAttnMaxGroup + g * kHeadDim + 32 * q + 8 * t4;
+                reinterpret_cast<float4 *>(dst)[0] =
+                    make_float4(o[4 * q][0] + o[4 * q][2], o[4 * q + 1][0] + o[4 * q + 1][2],
+                                o[4 * q + 2][0] + o[4 * q + 2][2], o[4 * q + 3][0] + o[4 * q + 3][2]);
+                reinterpret_cast<float4 *>(dst)[1] =
+                    make_float4(o[4 * q][1] + o[4 * q][3], o[4 * q + 1][1] + o[4 * q + 1][3],
+                                o[4 * q + 2][1] + o[4 * q + 2][3], o[4 * q + 3][1] + o[4 * q + 3][3]);
+            }
+            if (t4 == 0) {
+                pc[g] = m_run;
+                pc[kAttnMaxGroup + g] = lt;
+            }
+        }
+    };
+    auto start = [&](int item) {
+        int r0;
+        locate(item, cn, ch, cc, r0, cr1);
+        const float *qb = a.q + (size_t)cn * kHd + (size_t)(ch * G + g) * kHeadDim + 4 * t4;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (g < G) v = __ldcg(reinterpret_cast<const float4 *>(qb + 16 * u));
+            qa[2 * u][0] = tf32_hi(v.x);
+            qa[2 * u][1] = tf32_lo(v.x);
+            qa[2 * u][2] = tf32_hi(v.y);
+            qa[2 * u][3] = tf32_lo(v.y);
+            qa[2 * u + 1][0] = tf32_hi(v.z);
+            qa[2 * u + 1][1] = tf32_lo(v.z);
+            qa[2 * u + 1][2] = tf32_hi(v.w);
+            qa[2 * u + 1][3] = tf32_lo(v.w);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        m_run = -INFINITY;
+        l_run = 0.f;
+    };
+    int k = 0;
+    bool failed = false;
+    for (;; k++) {
+        const int s = k % kTcStages;
+        if (!mbar_wait(&full[s], (k / kTcStages) & 1, &a.st->err, kErrFullWait)) {
+            failed = true;
+            break;
+        }
+        const int item = hdr_item[warp][s], t0 = hdr_row[warp][s];
+        if (item < 0) {  // end of this warp's stream (possibly before any item)
+            if (cur >= 0) finish();
+            break;
+        }
+        if (item != cur) {
+            if (cur >= 0) finish();
+            cur = item;
+            start(item);
+        }
+        if (k == 0 && threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 2] = global_ns();
+        const int nrows = min(kTcRows, cr1 - t0);
+        const float *Ks = reinterpret_cast<const float *>(ring + (size_t)s * kTcStageBytes);
+        const float *Vs = Ks + kTcRows * kTcKStride;
+        float sa[2][4], sb[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) sa[j][e] = sb[j][e] = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float4 kv = *reinterpret_cast<const float4 *>(Ks + (8 * j + g) * kTcKStride + 16 * u + 4 * t4);
+                mma_tf32(sa[j], qa[2 * u], tf32_hi(kv.x), tf32_hi(kv.y));
+                mma_tf32(sb[j], qa[2 * u], tf32_lo(kv.x), tf32_lo(kv.y));
+                mma_tf32(sa[j], qa[2 * u + 1], tf32_hi(kv.z), tf32_hi(kv.w));
+                mma_tf32(sb[j], qa[2 * u + 1], tf32_lo(kv.z), tf32_lo(kv.w));
+            }
+        // Scores of head g, rows 8j + 2t + e: (Q_hi K) + (Q_lo K).
+        float sc[4];
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const float v = (sa[j][e] + sb[j][e]) + (sa[j][2 + e] + sb[j][2 + e]);
+                sc[2 * j + e] = (8 * j + 2 * t4 + e < nrows && g < G) ? v * scale2 : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float corr = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+        float p[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) p[i] = sc[i] == -INFINITY ? 0.f : exp2f(sc[i] - m_new);
+        l_run = fmaf(l_run, corr, (p[0] + p[1]) + (p[2] + p[3]));
+        m_run = m_new;
+        if (__any_sync(0xffffffffu, g < G && corr != 1.f)) {  // rows of padded heads stay zero
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) o[i][e] *= corr;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const uint32_t pa[4] = {tf32_hi(p[2 * j]), tf32_lo(p[2 * j]), tf32_hi(p[2 * j + 1]), tf32_lo(p[2 * j + 1])};
+            const float *v0 = Vs + (8 * j + 2 * t4) * kTcVStride + 4 * g, *v1 = v0 + kTcVStride;
+            if (nrows < kTcRows)
+                tc_pv_step<true>(o, pa, v0, v1, 8 * j + 2 * t4 < nrows, 8 * j + 2 * t4 + 1 < nrows);
+            else
+                tc_pv_step<false>(o, pa, v0, v1, true, true);
+        }
+        // This stage's slot is read: the next copies may land in it.
+        __syncwarp();
+        produce();
+    }
+    if (failed)  // copies this warp issued must land before it leaves
+        for (int j = k + 1; j < produced; j++)
+            if (!mbar_wait(&full[j % kTcStages], (j / kTcStages) & 1, &a.st->err, kErrDrain)) break;
+    if (threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 3] = global_ns();
+    // The last CTA out resets the work counter for the next launch.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&a.work[1], 1u) == gridDim.x - 1) {
+            a.work[0] = 0u;
+            a.work[1] = 0u;
+        }
+    }
+}
+
+// Folds the chunk partials of (session blockIdx.x, KV head blockIdx.y) in
+// chunk order and writes the heads' output rows as BF16 hi/lo.
+struct MergeArgs {
+    BatchState *st;
+    const float *part;
+    uint16_t *oh, *ol;
+    int item_rows;
+};
+__global__ void __launch_bounds__(256) batch_attn_merge_kernel(MergeArgs a) {
+    constexpr int G = 6;
+    __shared__ float m_s[G][kAttnItemMax], w_s[G][kAttnItemMax], den_s[G];
+    pdl_trigger();
+    pdl_wait();
+    const int n = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    if (n >= a.st->n) return;
+    const int nchunks = (a.st->position[n] + a.item_rows) / a.item_rows;
+    const float *hp = a.part + ((size_t)n * 2 + h) * kAttnItemMax * kAttnPartialFloats;
+    // Per (head, chunk): the chunk's max and sum, then per head the weights
+    // e_c = 2^(m_c - M) and the denominator, in chunk order.
+    if (tid < G * nchunks) {
+        const int gq = tid / nchunks, c = tid % nchunks;
+        m_s[gq][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats + gq);
+        w_s[gq][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats + kAttnMaxGroup + gq);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int c = 0; c < nchunks; c++) M = fmaxf(M, m_s[tid][c]);
+        float den = 0.f;
+        for (int c = 0; c < nchunks; c++) {
+            const float e = m_s[tid][c] == -INFINITY ? 0.f : exp2f(m_s[tid][c] - M);
+            den = m_s[tid][c] == -INFINITY ? den : fmaf(e, w_s[tid][c], den);
+            w_s[tid][c] = e;
+        }
+        den_s[tid] = den;
+    }
+    __syncthreads();
+    for (int o = tid; o < G * kHeadDim; o += blockDim.x) {
+        const int gq = o / kHeadDim, d = o % kHeadDim;
+        const float *pa = hp + 2 * kAttnMaxGroup + gq * kHeadDim + d;
+        float av[kAttnItemMax];
+#pragma unroll
+        for (int c = 0; c < kAttnItemMax; c++) av[c] = c < nchunks ? __ldcg(pa + (size_t)c * kAttnPartialFloats) : 0.f;
+        float num = 0.f;
+#pragma unroll
+        for (int c = 0; c < kAttnItemMax; c++)
+            if (c < nchunks && m_s[gq][c] != -INFINITY) num = fmaf(w_s[gq][c], av[c], num);
+        uint16_t hi, lo;
+        split_bf16(__fdiv_rn(num, den_s[gq]), hi, lo);
+        a.oh[(size_t)n * kHd + (h * G + gq) * kHeadDim + d] = hi;
+        a.ol[(size_t)n * kHd + (h * G + gq) * kHeadDim + d] = lo;
     }
 }
 
@@ -704,6 +1079,7 @@ struct QwenB200Batch {
     Top2 *top_part;
     int cluster_qkv, cluster_o, cluster_down;  // split clusters (0: split K through global memory)
     int attn_item_rows;   // cache rows per attention work item
+    int attn_kernel;      // 0: tensor-core fragments + merge kernel; 1: CUDA-core flash-decoding
     TcmTop2 *log, *host_log;
     unsigned long long *trace;  // stage timeline (measurement only), or null
     int readout_tiles;
@@ -801,6 +1177,19 @@ void launch_rms(QwenB200Batch *b, const float *w, bool embed, bool copy_x, bool 
     launch(batch_rms_kernel, dim3(kBN), dim3(256), 0, stream(), pdl, a);
 }
 
+// The attention of `layer` for n sessions (and its merge, for the tensor-core kernel).
+void launch_attention(QwenB200Batch *b, int layer, int n, unsigned long long *trace, bool pdl) {
+    AttnArgs at = {b->st, b->q, layer, 1.0f / sqrtf((float)kHeadDim), b->attn_part, b->attn_counters, b->nh, b->nl,
+                   trace, b->attn_work + 2 * layer, b->attn_item_rows};
+    if (b->attn_kernel == 0) {
+        launch(batch_attn_tc_kernel, dim3(sm_count()), dim3(kTcWarps * 32), kTcAttnSmem, stream(), pdl, at);
+        MergeArgs ma = {b->st, b->attn_part, b->nh, b->nl, b->attn_item_rows};
+        launch(batch_attn_merge_kernel, dim3(n, 2), dim3(256), 0, stream(), true, ma);
+    } else {
+        launch(batch_attn_kernel, dim3(sm_count()), dim3(kBatchAttnThreads), kAttnSmem, stream(), pdl, at);
+    }
+}
+
 void launch_step(QwenB200Batch *b, int n) {
     const QwenB200Shape &s = b->s;
     const std::vector<QwenB200Layer> &L = *b->layers;
@@ -809,9 +1198,7 @@ void launch_step(QwenB200Batch *b, int n) {
         const LayerMaps &m = b->maps[l];
         EpiQkv qkv = {b->st, L[l].qb, L[l].kb, L[l].vb, b->rope_den, b->q, l};
         launch_split(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, kHd / kTcKBlock, qkv, true, b->cluster_qkv);
-        AttnArgs at = {b->st, b->q, l, 1.0f / sqrtf((float)kHeadDim), b->attn_part, b->attn_counters, b->nh, b->nl,
-                       nullptr, b->attn_work + 2 * l, b->attn_item_rows};
-        launch(batch_attn_kernel, dim3(sm_count()), dim3(kBatchAttnThreads), kAttnSmem, stream(), true, at);
+        launch_attention(b, l, n, nullptr, true);
         EpiResid o = {b->st, b->x};
         launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, true, b->cluster_o);
         launch_rms(b, L[l].post_norm, false, false, true);
@@ -911,6 +1298,8 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
         gemm_setup<EpiLogits>();
         gemm_setup<EpiStore>();
         TCM_CUDA(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem));
+        TCM_CUDA(cudaFuncSetAttribute(batch_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kTcAttnSmem));
     });
     QwenB200Batch *b = new QwenB200Batch();
     b->d = d;
@@ -965,7 +1354,8 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
     // dependency wait, so neighbouring layers must not share them.
     b->attn_work = (unsigned *)gpu_alloc((size_t)s.layers * 2 * 4);
     gpu_zero(b->attn_work, (size_t)s.layers * 2 * 4);
-    b->attn_item_rows = 1024;
+    b->attn_item_rows = kTcItemRowsDefault;
+    b->attn_kernel = 0;
     b->cluster_qkv = pick_cluster(16, kHd / kTcKBlock);
     b->cluster_o = pick_cluster(12, kHd / kTcKBlock);
     b->cluster_down = pick_cluster(12, kFf / kTcKBlock);
@@ -993,15 +1383,19 @@ int qwen_b200_batch_max(void) { return kBN; }
 
 int qwen_b200_batch_tune(QwenB200Batch *b, int key, int value) {
     if (!b) return -1;
+    if (key == 0 && (value < kAttnItemRowsMin || value > 2048 || value % kAttnRowsPerStage)) return -1;
+    if (key == 1 && value != 0 && value != 1) return -1;
+    if (key != 0 && key != 1) return -1;
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    for (auto &g : b->graphs) TCM_CUDA(cudaGraphExecDestroy(g.second));
+    b->graphs.clear();
     if (key == 0) {  // attention rows per work item
-        if (value < kAttnItemRowsMin || value > 2048 || value % kAttnRowsPerStage) return -1;
-        TCM_CUDA(cudaStreamSynchronize(stream()));
-        for (auto &g : b->graphs) TCM_CUDA(cudaGraphExecDestroy(g.second));
-        b->graphs.clear();
         b->attn_item_rows = value;
-        return 0;
+    } else {  // attention kernel, with its own default item size
+        b->attn_kernel = value;
+        b->attn_item_rows = value == 0 ? kTcItemRowsDefault : 1024;
     }
-    return -1;
+    return 0;
 }
 
 int qwen_b200_batch_cluster_capacity(int size) { return size >= 1 && size <= 16 ? cluster_capacity(size) : -1; }
@@ -1044,9 +1438,7 @@ float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSes
                 break;
             }
             case 1: {
-                AttnArgs at = {b->st, b->q, layer, 1.0f / sqrtf((float)kHeadDim), b->attn_part, b->attn_counters,
-                               b->nh, b->nl, b->trace, b->attn_work + 2 * layer, b->attn_item_rows};
-                launch(batch_attn_kernel, dim3(sm_count()), dim3(kBatchAttnThreads), kAttnSmem, stream(), false, at);
+                launch_attention(b, layer, n, b->trace, false);
                 break;
             }
             case 2: {

@@ -198,7 +198,10 @@ int qwen_b200_batch_trace_stage(QwenB200Batch *, int n, const QwenB200BatchSessi
  * the split-K cluster sizes the engine chose (0: split through global memory). */
 int qwen_b200_batch_cluster_capacity(int size);
 /* Tuning: key 0 = cache rows per attention work item (a multiple of 32 in
- * [256, 2048], default 1024). Returns 0, or -1 for an unknown key or value. */
+ * [256, 2048]); key 1 = the attention kernel: 0 tensor-core fragments (the
+ * default, items of 256 rows), 1 CUDA-core flash-decoding (items of 1024
+ * rows); choosing a kernel resets the item size to its default. Returns 0, or
+ * -1 for an unknown key or value. */
 int qwen_b200_batch_tune(QwenB200Batch *, int key, int value);
 int qwen_b200_batch_clusters(const QwenB200Batch *, int *qkv, int *o, int *down);
 
@@ -216,46 +219,6 @@ int qwen_b200_persistent(QwenB200Runner *, int mode);
  * shared-memory copies (default 0). Returns 0, or -1 for an unknown key or
  * value. */
 int qwen_b200_persistent_tune(QwenB200Runner *, int key, int value);
-/* Measurement aid: mean device time (ms) of one standalone launch of a step's
- * stage for these sessions: 0 q/k/v GEMM (appends this step's K/V rows), 1
- * attention, 2 O GEMM, 3 gate/up GEMM, 4 down GEMM, 5 vocabulary GEMM, 6
- * RMSNorm, of `layer`, over `reps` launches. */
-float qwen_b200_batch_time_stage(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
-                                 const int *positions, int stage, int layer, int reps);
-/* The same launch with a per-CTA timeline: host receives ctas x 8 global-timer
- * stamps (ns; GEMM: entry, producer released, first stage ready, last MMA
- * committed, epilogue released, first accumulator read, last tile stored,
- * exit; attention: entry, consumers released, first stage ready, done). */
-int qwen_b200_batch_trace_stage(QwenB200Batch *, int n, const QwenB200BatchSession *sessions, const int *tokens,
-                                const int *positions, int stage, int layer, unsigned long long *host, int ctas);
-/* How many thread-block clusters of `size` GEMM CTAs the GPU holds at once, and
- * the split-K cluster sizes the engine chose (0: split through global memory). */
-int qwen_b200_batch_cluster_capacity(int size);
-/* Tuning: key 0 = cache rows per attention work item (a multiple of 32 in
- * [256, 2048], default 1024). Returns 0, or -1 for an unknown key or value. */
-int qwen_b200_batch_tune(QwenB200Batch *, int key, int value);
-int qwen_b200_batch_clusters(const QwenB200Batch *, int *qkv, int *o, int *down);
-
-/* Kernel launches one token issues (for launch accounting). */
-int qwen_b200_launches_per_token(const QwenB200Runner *);
-/* Whole-token execution: 1 = one persistent cooperative launch per token (one
- * CTA per SM runs every layer and the readout, the weights streaming through
- * grid barriers; applies when every layer is dense and no ring is attached);
- * 0 = the token graph of per-stage kernels (the default: faster on B200 at the
- * measured contexts); -1 queries. Both give identical bits. Returns the mode in
- * force, or -1 (mode 1 where it does not apply). */
-int qwen_b200_persistent(QwenB200Runner *, int mode);
-/* Tuning of the persistent kernel: key 0 = how far (KB, 0..2048) each CTA's
- * producer prefetches its coming weight and cache rows into L2 ahead of its
- * shared-memory copies (default 0). Returns 0, or -1 for an unknown key or
- * value. */
-int qwen_b200_persistent_tune(QwenB200Runner *, int key, int value);
-/* Pipelining of the token graph's kernels, as bits: 1 = each kernel lets its
- * dependent launch start once its input vector is ready (default: at entry);
- * 2 = each weight producer keeps one shared-memory stage in flight at a time
- * (default: all free stages). -1 queries. Bits only change timing. Returns
- * the mode in force, or -1. */
-int qwen_b200_pipeline(QwenB200Runner *, int mode);
 /* Measurement aid: mean device time (ms, CUDA events) of one standalone launch
  * of fused stage `stage` of `layer` (0 q/k/v, 1 attention, 2 O projection,
  * 3 gate/up, 4 down, 5 readout) at `position`, over `reps` launches. On a ring

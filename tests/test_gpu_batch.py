@@ -12,6 +12,8 @@
 3. A session's results do not depend on the rest of the batch (bit for bit), a
    rollback replays bit for bit, and chained device-fed steps
    (qwen_b200_batch_enqueue) equal step-by-step pushes bit for bit.
+4. The tensor-core attention kernel against the CUDA-core one on the same
+   caches (1 to 8,190 rows), at two work-item sizes.
 """
 import ctypes
 
@@ -108,6 +110,56 @@ def test_batch_full_depth_matches_oracle():
     worst, kv, agree, forced = run_batch_parity(28, 82, [3, 8, 1, 12], 14, 16)
     print(f"batch 4, 28 layers: max|dlogit|={worst:.3e} max|dkv|={kv:.3e} agree={agree} forced={forced}")
     assert worst <= BF16_TOL and kv <= BF16_TOL
+
+
+def test_tensor_core_attention_matches_cuda_core_attention():
+    """The batched attention on tensor-core fragments (the default: TF32 hi/lo
+    operand splits, 256-row items, a separate merge) against the CUDA-core
+    flash-decoding kernel, on the same seeded caches: contexts from 1 row to
+    8,190 (partial 16-row stages, one and many items per session), one step
+    of a 2-layer model. Logits agree to the path's FP32 rounding level (the
+    attention output enters the O projection as BF16 hi/lo, about 2^-17)."""
+    L = cm.lib()
+    shape = cm.qwen_shape(2, 9216)
+    model = cm.Model(shape, 84, cm.TEST_LAW, 2)
+    lengths = [1, 7, 16, 17, 255, 256, 257, 1000, 3001, 4096, 5000, 8190]
+    n = len(lengths)
+    rng = np.random.default_rng(84)
+    sessions = []
+    for i, ln in enumerate(lengths):
+        s = cm.Session(model, ln + 2)
+        v = s.view()
+        count = shape.layers * shape.kvheads * v.capacity * shape.head
+        L.qwen_b200_seeded_fill(ctypes.c_void_p(v.keys), 1, 77, 200 + 2 * i, count, 0.0, 0.8)
+        L.qwen_b200_seeded_fill(ctypes.c_void_p(v.values), 1, 77, 201 + 2 * i, count, 0.0, 0.8)
+        assert L.qwen_b200_session_set_cursor(s.handle, ln, int(rng.integers(0, shape.vocab))) == 0
+        sessions.append(s)
+    batch = L.qwen_b200_batch_create(L.qwen_b200_model_decoder(model.handle))
+    try:
+        views = [s.view() for s in sessions]
+        bs = (cm.BatchSession * n)(*[cm.BatchSession(v.keys, v.values, v.capacity, v.logits, v.x) for v in views])
+        cp = (ctypes.c_int * n)(*[v.position for v in views])
+        ct = (ctypes.c_int * n)(*[v.pending for v in views])
+        tops = (cm.Top2 * n)()
+        out = {}
+        for kernel, rows in ((1, 1024), (0, 256), (0, 512)):
+            assert L.qwen_b200_batch_tune(batch, 1, kernel) == 0
+            assert L.qwen_b200_batch_tune(batch, 0, rows) == 0
+            assert L.qwen_b200_batch_enqueue(batch, n, bs, ct, cp, 1) == 0
+            assert L.qwen_b200_batch_read(batch, n, 1, tops, None) == 0
+            out[(kernel, rows)] = [s.logits().copy() for s in sessions]
+        ref = out[(1, 1024)]
+        scale = max(float(np.max(np.abs(r))) for r in ref)
+        for key in ((0, 256), (0, 512)):
+            err = max(float(np.max(np.abs(a - b))) for a, b in zip(out[key], ref))
+            print(f"attention kernel {key}: max|dlogit| {err:.3e} (logit scale {scale:.3e})")
+            assert err <= 1e-4 * max(scale, 1.0)
+        assert L.qwen_b200_batch_tune(batch, 1, 2) == -1
+    finally:
+        L.qwen_b200_batch_free(batch)
+        for s in sessions:
+            s.free()
+        model.free()
 
 
 def test_batch_composition_rollback_and_chained_steps():
