@@ -474,10 +474,12 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
                    "l2": "inputs larger than L2 (weights and K/V stream from HBM every step)"},
         "e2e": {"value": round(e2e_steps * n * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * 16},
-        "gpu_launches": (shape.layers * 7 + 4) * (steps + max(args.warmup, 3)),
-        "roofline": {"bound": "hbm", "kernel": "batch_attn_kernel (64 sessions x 2 KV heads, split-K flash decoding)",
+        "gpu_launches": (shape.layers * 8 + 4) * (steps + max(args.warmup, 3)),
+        "roofline": {"bound": "hbm",
+                     "kernel": "batch_attn_tc_kernel + batch_attn_merge_kernel (64 sessions x 2 KV heads, "
+                               "split-K flash decoding on TF32 tensor-core fragments)",
                      "achieved": round(attn_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(attn_gbs / peak, 4),
-                     "peak_source": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": int(attn_bytes),
+                     "peak_source": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": int(attn_bytes),
                      "launch_ms": round(stage["attention"], 5)},
         "tensor_roofline": {"bound": "tensor", "kernels": "tc_gemm_kernel (q/k/v, O, gate/up, down of one layer)",
                             "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",

@@ -276,7 +276,7 @@ __global__ void split_rows_kernel(const float *x, uint16_t *hi, uint16_t *lo, si
 constexpr int kAttnRowsPerStage = 32;                  // 8 warps x 4 rows
 constexpr int kAttnStageBytes = 2 * kAttnRowsPerStage * kHeadDim * 4;  // K and V: 32 KB
 constexpr int kAttnRingStages = 6;
-constexpr int kAttnItemRowsMin = 256;   // item sizes are multiples of 32 rows in [256, 2048]
+constexpr int kAttnItemRowsMin = 128;   // item sizes are multiples of 32 rows in [128, 2048]
 constexpr int kAttnItemMax = (kAttnSplitMax * kAttnChunk) / kAttnItemRowsMin;  // chunks per (session, head)
 constexpr size_t kAttnSmem = ring_smem_bytes(kAttnRingStages, kAttnStageBytes);
 
@@ -589,7 +589,7 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
 // The same work items, with the arithmetic on the tensor cores (mma.sync
 // m16n8k8, TF32 operands, FP32 accumulation) and no sharing between warps:
 // each of the CTA's four warps takes whole items from the global counter and
-// feeds itself through its own three stages of 16 K rows and 16 V rows (each
+// feeds itself through its own three stages of 8 K rows and 8 V rows (each
 // lane moves 16-byte pieces with cp.async; K rows land 576 bytes apart and V
 // rows 528, so every fragment load below is free of bank conflicts; a stage's
 // barrier completes when all 32 lanes' pieces have landed), issuing the next
@@ -603,21 +603,25 @@ __global__ void __launch_bounds__(kBatchAttnThreads, 1) batch_attn_kernel(AttnAr
 //     each k-step of 8 is permuted (lane slot t <-> dimension 4t, slot t + 4
 //     <-> 4t + 1 of a 16-dimension block), identically for A and B;
 //   online softmax in base 2 on the accumulator layout: lane (g, t) holds
-//     head g's scores of rows 2t and 2t + 1 of each 8-row tile;
+//     head g's scores of rows 2t and 2t + 1 of the 8-row tile; the reference
+//     max a head's exponentials use moves only when the tile's max exceeds
+//     it by more than kTcLazy (then the accumulators are rescaled), so
+//     exponentials stay below 2^kTcLazy and most tiles need no rescale;
 //   O += P V: A = [P_hi; P_lo] straight from those registers (row slot t <->
 //     row 2t, slot t + 4 <-> 2t + 1), B = V_hi and then V_lo.
 // x_hi keeps the TF32 bits of x and x_lo = x - x_hi (exact), so every product
 // carries about 21 bits of each operand: FP32-level scores and outputs.
 // Each item leaves a partial (max, sum, accumulators) in global memory, and
 // batch_attn_merge_kernel folds a (session, head)'s partials in chunk order.
-constexpr int kTcWarps = 4;
-constexpr int kTcRows = 16;                // cache rows per stage
+constexpr int kTcWarps = 8;
+constexpr int kTcRows = 8;                 // cache rows per stage (one 8-row tile)
 constexpr int kTcStages = 3;               // stages per warp
 constexpr int kTcKStride = kHeadDim + 16;  // K row stride in floats (576 bytes)
 constexpr int kTcVStride = kHeadDim + 4;   // V row stride in floats (528 bytes)
 constexpr uint32_t kTcStageBytes = (uint32_t)kTcRows * (kTcKStride + kTcVStride) * 4;
 constexpr size_t kTcAttnSmem = (size_t)kTcWarps * kTcStages * kTcStageBytes + (size_t)kTcWarps * kTcStages * 8;
 constexpr int kTcItemRowsDefault = 256;
+constexpr float kTcLazy = 8.f;             // base-2 headroom of the softmax's reference max
 static_assert(kTcAttnSmem <= 227 * 1024, "shared memory");
 
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -662,7 +666,8 @@ __device__ __forceinline__ void tc_pv_step(float (&o)[16][4], const uint32_t (&p
 __global__ void __launch_bounds__(kTcWarps * 32, 1) batch_attn_tc_kernel(AttnArgs a) {
     constexpr int G = 6;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ int chunk_start[kBN + 1], fresh_s[kBN];
+    __shared__ int chunk_start[kBN + 1], fresh_s[kBN], pos_s[kBN];
+    __shared__ const float *keys_s[kBN];
     __shared__ int hdr_item[kTcWarps][kTcStages], hdr_row[kTcWarps][kTcStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     unsigned char *ring = smem + (size_t)warp * kTcStages * kTcStageBytes;
@@ -673,31 +678,54 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) batch_attn_tc_kernel(AttnArg
     }
     pdl_trigger();
     if (threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 0] = global_ns();
+    // Items are numbered with every (session, head)'s chunks but its last
+    // first, session by session (chunk_start: prefix of 2 (chunks - 1)), then
+    // the last chunks (n, h) -- the short ones -- so the warps that finish
+    // last take the smallest items.
+    // The sessions' positions and cache pointers are read once (one load per
+    // thread), then the per-session quantities come from shared memory.
     const int n_active = a.st->n;
+    if ((int)threadIdx.x < n_active) {
+        pos_s[threadIdx.x] = a.st->position[threadIdx.x];
+        keys_s[threadIdx.x] = a.st->keys[threadIdx.x];
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < n_active) {
+        const int n = threadIdx.x;
+        int fresh = pos_s[n];  // first_fresh_row, from the staged copies
+        for (int m = 0; m < n_active; m++)
+            if (keys_s[m] == keys_s[n]) fresh = min(fresh, pos_s[m]);
+        fresh_s[n] = fresh;
+    }
     if (threadIdx.x == 0) {
         int acc_items = 0;
         for (int n = 0; n < n_active; n++) {
             chunk_start[n] = acc_items;
-            acc_items += 2 * ((a.st->position[n] + a.item_rows) / a.item_rows);
+            acc_items += 2 * ((pos_s[n] + a.item_rows) / a.item_rows - 1);
         }
         chunk_start[n_active] = acc_items;
     }
-    if ((int)threadIdx.x < n_active) fresh_s[threadIdx.x] = first_fresh_row(a.st, n_active, threadIdx.x);
     __syncthreads();
-    const int items = chunk_start[n_active];
+    const int full_items = chunk_start[n_active], items = full_items + 2 * n_active;
     auto locate = [&](int item, int &n, int &h, int &c, int &rows0, int &rows1) {
-        int lo = 0, hi = n_active - 1;  // last session with chunk_start <= item
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (chunk_start[mid] <= item) lo = mid;
-            else hi = mid - 1;
+        if (item >= full_items) {
+            n = (item - full_items) >> 1;
+            h = (item - full_items) & 1;
+            c = (pos_s[n] + a.item_rows) / a.item_rows - 1;
+        } else {
+            int lo = 0, hi = n_active - 1;  // last session with chunk_start <= item
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (chunk_start[mid] <= item) lo = mid;
+                else hi = mid - 1;
+            }
+            n = lo;
+            const int within = item - chunk_start[n], chunks = (chunk_start[n + 1] - chunk_start[n]) / 2;
+            h = within / chunks;
+            c = within % chunks;
         }
-        n = lo;
-        const int within = item - chunk_start[n], chunks = (chunk_start[n + 1] - chunk_start[n]) / 2;
-        h = within / chunks;
-        c = within % chunks;
         rows0 = c * a.item_rows;
-        rows1 = min(a.st->position[n] + 1, rows0 + a.item_rows);
+        rows1 = min(pos_s[n] + 1, rows0 + a.item_rows);
     };
 
     // Producer side (warp-uniform state): the item being copied and its next row.
@@ -825,52 +853,51 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) batch_attn_tc_kernel(AttnArg
         const int nrows = min(kTcRows, cr1 - t0);
         const float *Ks = reinterpret_cast<const float *>(ring + (size_t)s * kTcStageBytes);
         const float *Vs = Ks + kTcRows * kTcKStride;
+        // S = [Q_hi; Q_lo] (K_hi + K_lo)^T in four accumulator chains (K_hi or
+        // K_lo, even or odd 16-dimension block).
         float sa[2][4], sb[2][4];
 #pragma unroll
-        for (int j = 0; j < 2; j++)
+        for (int c = 0; c < 2; c++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) sa[j][e] = sb[j][e] = 0.f;
+            for (int e = 0; e < 4; e++) sa[c][e] = sb[c][e] = 0.f;
 #pragma unroll
-        for (int u = 0; u < 8; u++)
+        for (int u = 0; u < 8; u++) {
+            const float4 kv = *reinterpret_cast<const float4 *>(Ks + g * kTcKStride + 16 * u + 4 * t4);
+            mma_tf32(sa[u & 1], qa[2 * u], tf32_hi(kv.x), tf32_hi(kv.y));
+            mma_tf32(sb[u & 1], qa[2 * u], tf32_lo(kv.x), tf32_lo(kv.y));
+            mma_tf32(sa[u & 1], qa[2 * u + 1], tf32_hi(kv.z), tf32_hi(kv.w));
+            mma_tf32(sb[u & 1], qa[2 * u + 1], tf32_lo(kv.z), tf32_lo(kv.w));
+        }
+        // Scores of head g, rows 2t + e: (Q_hi K) + (Q_lo K).
+        float sc[2];
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const float4 kv = *reinterpret_cast<const float4 *>(Ks + (8 * j + g) * kTcKStride + 16 * u + 4 * t4);
-                mma_tf32(sa[j], qa[2 * u], tf32_hi(kv.x), tf32_hi(kv.y));
-                mma_tf32(sb[j], qa[2 * u], tf32_lo(kv.x), tf32_lo(kv.y));
-                mma_tf32(sa[j], qa[2 * u + 1], tf32_hi(kv.z), tf32_hi(kv.w));
-                mma_tf32(sb[j], qa[2 * u + 1], tf32_lo(kv.z), tf32_lo(kv.w));
-            }
-        // Scores of head g, rows 8j + 2t + e: (Q_hi K) + (Q_lo K).
-        float sc[4];
-#pragma unroll
-        for (int j = 0; j < 2; j++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const float v = (sa[j][e] + sb[j][e]) + (sa[j][2 + e] + sb[j][2 + e]);
-                sc[2 * j + e] = (8 * j + 2 * t4 + e < nrows && g < G) ? v * scale2 : -INFINITY;
-            }
-        float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+        for (int e = 0; e < 2; e++) {
+            const float hi = (sa[0][e] + sa[1][e]) + (sb[0][e] + sb[1][e]);
+            const float lo = (sa[0][2 + e] + sa[1][2 + e]) + (sb[0][2 + e] + sb[1][2 + e]);
+            sc[e] = (2 * t4 + e < nrows && g < G) ? (hi + lo) * scale2 : -INFINITY;
+        }
+        float mx = fmaxf(sc[0], sc[1]);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float corr = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
-        float p[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) p[i] = sc[i] == -INFINITY ? 0.f : exp2f(sc[i] - m_new);
-        l_run = fmaf(l_run, corr, (p[0] + p[1]) + (p[2] + p[3]));
-        m_run = m_new;
-        if (__any_sync(0xffffffffu, g < G && corr != 1.f)) {  // rows of padded heads stay zero
+        if (__any_sync(0xffffffffu, g < G && (m_run == -INFINITY ? mx != -INFINITY : mx > m_run + kTcLazy))) {
+            const float m_new = (m_run == -INFINITY || mx > m_run + kTcLazy) ? fmaxf(m_run, mx) : m_run;
+            const float corr = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+            l_run *= corr;
 #pragma unroll
             for (int i = 0; i < 16; i++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) o[i][e] *= corr;
+            m_run = m_new;
         }
+        float p[2];
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const uint32_t pa[4] = {tf32_hi(p[2 * j]), tf32_lo(p[2 * j]), tf32_hi(p[2 * j + 1]), tf32_lo(p[2 * j + 1])};
-            const float *v0 = Vs + (8 * j + 2 * t4) * kTcVStride + 4 * g, *v1 = v0 + kTcVStride;
+        for (int e = 0; e < 2; e++) p[e] = sc[e] == -INFINITY ? 0.f : exp2f(sc[e] - m_run);
+        l_run += p[0] + p[1];
+        {
+            const uint32_t pa[4] = {tf32_hi(p[0]), tf32_lo(p[0]), tf32_hi(p[1]), tf32_lo(p[1])};
+            const float *v0 = Vs + 2 * t4 * kTcVStride + 4 * g, *v1 = v0 + kTcVStride;
             if (nrows < kTcRows)
-                tc_pv_step<true>(o, pa, v0, v1, 8 * j + 2 * t4 < nrows, 8 * j + 2 * t4 + 1 < nrows);
+                tc_pv_step<true>(o, pa, v0, v1, 2 * t4 < nrows, 2 * t4 + 1 < nrows);
             else
                 tc_pv_step<false>(o, pa, v0, v1, true, true);
         }
@@ -882,11 +909,11 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) batch_attn_tc_kernel(AttnArg
         for (int j = k + 1; j < produced; j++)
             if (!mbar_wait(&full[j % kTcStages], (j / kTcStages) & 1, &a.st->err, kErrDrain)) break;
     if (threadIdx.x == 0 && a.trace) a.trace[(size_t)blockIdx.x * 8 + 3] = global_ns();
-    // The last CTA out resets the work counter for the next launch.
-    __syncthreads();
-    if (threadIdx.x == 0) {
+    // The last warp out (every warp has drawn past the last item) resets the
+    // work counter for the next launch; no warp waits for the others.
+    if (lane == 0) {
         __threadfence();
-        if (atomicAdd(&a.work[1], 1u) == gridDim.x - 1) {
+        if (atomicAdd(&a.work[1], 1u) == gridDim.x * kTcWarps - 1) {
             a.work[0] = 0u;
             a.work[1] = 0u;
         }
@@ -912,8 +939,8 @@ __global__ void __launch_bounds__(256) batch_attn_merge_kernel(MergeArgs a) {
     const float *hp = a.part + ((size_t)n * 2 + h) * kAttnItemMax * kAttnPartialFloats;
     // Per (head, chunk): the chunk's max and sum, then per head the weights
     // e_c = 2^(m_c - M) and the denominator, in chunk order.
-    if (tid < G * nchunks) {
-        const int gq = tid / nchunks, c = tid % nchunks;
+    for (int i = tid; i < G * nchunks; i += blockDim.x) {
+        const int gq = i / nchunks, c = i % nchunks;
         m_s[gq][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats + gq);
         w_s[gq][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats + kAttnMaxGroup + gq);
     }

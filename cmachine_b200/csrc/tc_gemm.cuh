@@ -346,7 +346,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const int e = (warp & 3) * 32 + lane;
             // Sums of the slice in registers: S >= 4 gives at most 16 pairs, 2 rows
             // each, N columns, over 128 threads.
+            // Each element's S remote values are all requested before they are
+            // added (in rank order): one distributed-shared-memory round trip
+            // per element instead of S.
             constexpr int kMaxPer = (16 * 2 * N + 127) / 128;
+            constexpr int kMaxRanks = 16;
             float sum[kMaxPer];
 #pragma unroll
             for (int j = 0; j < kMaxPer; j++) {
@@ -355,7 +359,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 if (idx < count) {
                     const int pr = idx / (2 * N), rem = idx % (2 * N), half = rem / N, c = rem % N;
                     const int row = p0 + pr + 64 * half;
-                    for (int q = 0; q < S; q++) sum[j] += cluster.map_shared_rank(&tile[row][c], q)[0];
+                    float part[kMaxRanks];
+#pragma unroll
+                    for (int q = 0; q < kMaxRanks; q++)
+                        part[q] = q < S ? cluster.map_shared_rank(&tile[row][c], q)[0] : 0.f;
+#pragma unroll
+                    for (int q = 0; q < kMaxRanks; q++)
+                        if (q < S) sum[j] += part[q];
                 }
             }
             cluster.sync();  // every rank has read every partial it needs
