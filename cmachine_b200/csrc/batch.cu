@@ -276,7 +276,7 @@ __global__ void split_rows_kernel(const float *x, uint16_t *hi, uint16_t *lo, si
 constexpr int kAttnRowsPerStage = 32;                  // 8 warps x 4 rows
 constexpr int kAttnStageBytes = 2 * kAttnRowsPerStage * kHeadDim * 4;  // K and V: 32 KB
 constexpr int kAttnRingStages = 6;
-constexpr int kAttnItemRowsMin = 128;   // item sizes are multiples of 32 rows in [128, 2048]
+constexpr int kAttnItemRowsMin = 256;   // item sizes are multiples of 32 rows in [256, 2048]
 constexpr int kAttnItemMax = (kAttnSplitMax * kAttnChunk) / kAttnItemRowsMin;  // chunks per (session, head)
 constexpr size_t kAttnSmem = ring_smem_bytes(kAttnRingStages, kAttnStageBytes);
 
@@ -929,7 +929,7 @@ struct MergeArgs {
     int item_rows;
 };
 __global__ void __launch_bounds__(256) batch_attn_merge_kernel(MergeArgs a) {
-    constexpr int G = 6;
+    constexpr int G = 6, kPer = G * kHeadDim / 256;  // outputs per thread
     __shared__ float m_s[G][kAttnItemMax], w_s[G][kAttnItemMax], den_s[G];
     pdl_trigger();
     pdl_wait();
@@ -937,14 +937,24 @@ __global__ void __launch_bounds__(256) batch_attn_merge_kernel(MergeArgs a) {
     if (n >= a.st->n) return;
     const int nchunks = (a.st->position[n] + a.item_rows) / a.item_rows;
     const float *hp = a.part + ((size_t)n * 2 + h) * kAttnItemMax * kAttnPartialFloats;
-    // Per (head, chunk): the chunk's max and sum, then per head the weights
-    // e_c = 2^(m_c - M) and the denominator, in chunk order.
+    // Every load is issued before any arithmetic: this thread's outputs
+    // o = tid + 256 k over all chunks, and per (head, chunk) the chunk's max
+    // and sum into shared memory.
+    float av[kPer][kAttnItemMax];
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+        const int o = tid + 256 * k;
+        const float *pa = hp + 2 * kAttnMaxGroup + (o / kHeadDim) * kHeadDim + o % kHeadDim;
+#pragma unroll
+        for (int c = 0; c < kAttnItemMax; c++) av[k][c] = c < nchunks ? __ldcg(pa + (size_t)c * kAttnPartialFloats) : 0.f;
+    }
     for (int i = tid; i < G * nchunks; i += blockDim.x) {
         const int gq = i / nchunks, c = i % nchunks;
         m_s[gq][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats + gq);
         w_s[gq][c] = __ldcg(hp + (size_t)c * kAttnPartialFloats + kAttnMaxGroup + gq);
     }
     __syncthreads();
+    // Per head: the weights e_c = 2^(m_c - M) and the denominator, in chunk order.
     if (tid < G) {
         float M = -INFINITY;
         for (int c = 0; c < nchunks; c++) M = fmaxf(M, m_s[tid][c]);
@@ -957,16 +967,13 @@ __global__ void __launch_bounds__(256) batch_attn_merge_kernel(MergeArgs a) {
         den_s[tid] = den;
     }
     __syncthreads();
-    for (int o = tid; o < G * kHeadDim; o += blockDim.x) {
-        const int gq = o / kHeadDim, d = o % kHeadDim;
-        const float *pa = hp + 2 * kAttnMaxGroup + gq * kHeadDim + d;
-        float av[kAttnItemMax];
 #pragma unroll
-        for (int c = 0; c < kAttnItemMax; c++) av[c] = c < nchunks ? __ldcg(pa + (size_t)c * kAttnPartialFloats) : 0.f;
+    for (int k = 0; k < kPer; k++) {
+        const int o = tid + 256 * k, gq = o / kHeadDim, d = o % kHeadDim;
         float num = 0.f;
 #pragma unroll
         for (int c = 0; c < kAttnItemMax; c++)
-            if (c < nchunks && m_s[gq][c] != -INFINITY) num = fmaf(w_s[gq][c], av[c], num);
+            if (c < nchunks && m_s[gq][c] != -INFINITY) num = fmaf(w_s[gq][c], av[k][c], num);
         uint16_t hi, lo;
         split_bf16(__fdiv_rn(num, den_s[gq]), hi, lo);
         a.oh[(size_t)n * kHd + (h * G + gq) * kHeadDim + d] = hi;

@@ -337,51 +337,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     }
     if (a.cluster > 1) {
         // Cluster fold: rank r owns row pairs [r * 64 / S, (r + 1) * 64 / S).
+        // After the first barrier every rank's MMAs are done, so its operand
+        // ring is idle: each rank writes every row of its partial tile into
+        // the ring of the rank that owns the row (posted remote stores,
+        // receive layout [source rank][row of the owner's slice][N + 4]).
+        // After the second barrier each owner adds its S received slices in
+        // rank order, from its own shared memory.
         namespace cg = cooperative_groups;
         cg::cluster_group cluster = cg::this_cluster();
+        constexpr int kRS = N + 4;  // receive row stride (floats; 16-byte rows)
+        // S x 2 ceil(64 / S) <= 150 receive rows for every cluster size S <= 16.
+        static_assert((size_t)150 * kRS * 4 <= (size_t)G::kStages * G::kStage, "cluster receive buffer");
+        const int S = a.cluster, r = (int)cluster.block_rank(), t = blockIdx.x / S;
+        const int npmax = (64 + S - 1) / S;
+        const int e = (warp & 3) * 32 + lane;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the ring's async-proxy use is over
         cluster.sync();
         if (warp >= 2) {
-            const int S = a.cluster, r = (int)cluster.block_rank(), t = blockIdx.x / S;
-            const int p0 = r * 64 / S, p1 = (r + 1) * 64 / S, count = (p1 - p0) * 2 * N;
-            const int e = (warp & 3) * 32 + lane;
-            // Sums of the slice in registers: S >= 4 gives at most 16 pairs, 2 rows
-            // each, N columns, over 128 threads.
-            // Each element's S remote values are all requested before they are
-            // added (in rank order): one distributed-shared-memory round trip
-            // per element instead of S.
-            constexpr int kMaxPer = (16 * 2 * N + 127) / 128;
-            constexpr int kMaxRanks = 16;
-            float sum[kMaxPer];
+            const int pr = e & 63, half = e >> 6;
+            int o = 0;
+            while (o + 1 < S && (o + 1) * 64 / S <= pr) o++;
+            const int op0 = o * 64 / S, onp = (o + 1) * 64 / S - op0;
+            float *dst = cluster.map_shared_rank(reinterpret_cast<float *>(smem), o) +
+                         ((size_t)r * 2 * npmax + (pr - op0) + half * onp) * kRS;
 #pragma unroll
-            for (int j = 0; j < kMaxPer; j++) {
-                const int idx = e + 128 * j;
-                sum[j] = 0.f;
-                if (idx < count) {
-                    const int pr = idx / (2 * N), rem = idx % (2 * N), half = rem / N, c = rem % N;
-                    const int row = p0 + pr + 64 * half;
-                    float part[kMaxRanks];
+            for (int c = 0; c < N; c += 4)
+                *reinterpret_cast<float4 *>(dst + c) = make_float4(tile[e][c], tile[e][c + 1], tile[e][c + 2], tile[e][c + 3]);
+        }
+        cluster.sync();  // every row has reached its owner
+        if (warp >= 2) {
+            const int p0 = r * 64 / S, p1 = (r + 1) * 64 / S, np = p1 - p0, count = 2 * np * N;
+            const float *recv = reinterpret_cast<const float *>(smem);
+            for (int idx = e; idx < count; idx += 128) {
+                const int jr = idx / N, c = idx % N;
+                float part[16];  // all of the element's slices requested first
 #pragma unroll
-                    for (int q = 0; q < kMaxRanks; q++)
-                        part[q] = q < S ? cluster.map_shared_rank(&tile[row][c], q)[0] : 0.f;
-#pragma unroll
-                    for (int q = 0; q < kMaxRanks; q++)
-                        if (q < S) sum[j] += part[q];
+                for (int q = 0; q < 16; q++) {
+                    part[q] = 0.f;
+                    if (q < S)
+                        asm volatile("ld.shared.f32 %0, [%1];"
+                                     : "=f"(part[q])
+                                     : "r"(smem_addr(recv + ((size_t)q * 2 * npmax + jr) * kRS + c)));
                 }
-            }
-            cluster.sync();  // every rank has read every partial it needs
+                float sum = 0.f;
 #pragma unroll
-            for (int j = 0; j < kMaxPer; j++) {
-                const int idx = e + 128 * j;
-                if (idx < count) {
-                    const int pr = idx / (2 * N), rem = idx % (2 * N), half = rem / N, c = rem % N;
-                    tile[p0 + pr + 64 * half][c] = sum[j];
-                }
+                for (int q = 0; q < 16; q++)
+                    if (q < S) sum += part[q];
+                tile[jr < np ? p0 + jr : 64 + p0 + (jr - np)][c] = sum;
             }
             epi_sync();
             a.epi.store(t, tile, p0, p1, e, scratch);
             if (e == 0) tc_mark(a.trace, 6);
-        } else {
-            cluster.sync();
         }
     }
     tc_fence_before();

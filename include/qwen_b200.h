@@ -198,7 +198,7 @@ int qwen_b200_batch_trace_stage(QwenB200Batch *, int n, const QwenB200BatchSessi
  * the split-K cluster sizes the engine chose (0: split through global memory). */
 int qwen_b200_batch_cluster_capacity(int size);
 /* Tuning: key 0 = cache rows per attention work item (a multiple of 32 in
- * [128, 2048]); key 1 = the attention kernel: 0 tensor-core fragments (the
+ * [256, 2048]); key 1 = the attention kernel: 0 tensor-core fragments (the
  * default, items of 256 rows), 1 CUDA-core flash-decoding (items of 1024
  * rows); choosing a kernel resets the item size to its default. Returns 0, or
  * -1 for an unknown key or value. */
