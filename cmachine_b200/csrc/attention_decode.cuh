@@ -11,10 +11,10 @@
 // reduce-scatter butterfly leaves one full score per lane; the online softmax
 // then updates each head's running max and rescaled sum, and the accumulators
 // take the probabilities by shuffle. The warps merge in a fixed order into the
-// CTA's partial in shared memory; after a cluster barrier every CTA reads all
-// partials of its cluster (DSMEM) for its share of the outputs and folds them
-// in rank order (deterministic); a second barrier keeps the partials alive
-// until all reads are done. With several clusters per head, their partials
+// CTA's partial in shared memory; every CTA then writes each rank the part of
+// its partial that rank folds (distributed shared memory stores), and after one
+// cluster barrier each rank folds its share of the outputs from its own shared
+// memory in rank order (deterministic). With several clusters per head, their partials
 // meet in global memory and the last CTA to arrive folds them in order.
 // Scores are dot * (1 / sqrt(128)), the reference's GPU scaling
 // (src/qwen_cuda.cu:70).
@@ -395,6 +395,8 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
     __shared__ __align__(16) float cta_part[kAttnPartialFloats];
+    constexpr int kRecvFloats = 2 * kAttnMaxGroup + G * kHeadDim / kCluster;  // 64: what one rank sends another
+    __shared__ __align__(16) float recv_s[kCluster][kRecvFloats];
     __shared__ int last_s;
     __shared__ __align__(8) uint64_t kv_bar;
     extern __shared__ __align__(128) unsigned char staged[];  // [K rows][V rows], kStagedRows each (DenseRows)
@@ -488,9 +490,22 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     // This CTA's slice result into shared memory, then the cluster combine:
     // rank r folds the cluster's partials for outputs [r * kOutPer, ...).
     cta_merge<G>(m, l, acc, wm, wl, wacc, cta_part, nullptr, [] { __syncthreads(); });
-    cluster.sync();
     constexpr int kOutPer = G * kHeadDim / kCluster;
     static_assert(G * kHeadDim % kCluster == 0 && kOutPer <= kDecodeAttnThreads, "cluster output split");
+    static_assert(kCluster * 16 == kDecodeAttnThreads && kOutPer == 48, "one 16-byte piece per thread");
+    // Each CTA sends every rank r what r folds: the maxima and sums (16
+    // floats) and its accumulators for outputs [r * kOutPer, ...) (contiguous
+    // in the partial), as posted remote stores into r's recv_s row of this
+    // CTA; after one cluster barrier every rank folds from its own shared
+    // memory and no CTA touches another's again.
+    __syncthreads();  // this CTA's partial is complete
+    {
+        const int q = tid >> 4, c = tid & 15;
+        const float *src = c < 4 ? cta_part + 4 * c : cta_part + 2 * kAttnMaxGroup + q * kOutPer + 4 * (c - 4);
+        float *dst = cluster.map_shared_rank(&recv_s[0][0], q) + rank * kRecvFloats + 4 * c;
+        *reinterpret_cast<float4 *>(dst) = *reinterpret_cast<const float4 *>(src);
+    }
+    cluster.sync();
     // Deferred (defer != 0): every used cluster leaves its partial in `part`
     // and the next launch folds them (unused clusters' partials are marked
     // empty); `out` and `counters` are not touched.
@@ -500,10 +515,9 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
         float mr[kCluster], lr[kCluster], ar[kCluster];
 #pragma unroll
         for (int r = 0; r < kCluster; r++) {
-            const float *pr = cluster.map_shared_rank(cta_part, r);
-            mr[r] = pr[g];
-            lr[r] = pr[kAttnMaxGroup + g];
-            ar[r] = pr[2 * kAttnMaxGroup + g * kHeadDim + d];
+            mr[r] = recv_s[r][g];
+            lr[r] = recv_s[r][kAttnMaxGroup + g];
+            ar[r] = recv_s[r][2 * kAttnMaxGroup + tid];
         }
         float M = -INFINITY;
 #pragma unroll
@@ -528,7 +542,6 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
         const int c = 1 + tid / kAttnMaxGroup, g = tid % kAttnMaxGroup;
         part[((size_t)kvh * clusters + c) * kAttnPartialFloats + g] = -INFINITY;
     }
-    cluster.sync();  // no CTA leaves while another still reads its partial
     if (multi && !defer) {
         // The last CTA of the head to arrive merges the clusters' partials.
         __threadfence();
