@@ -420,6 +420,10 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
         if (mark && tid == 0) mark[0] = 0ull;  // no work: not part of the timeline
         return;
     }
+    // First phase of a cluster barrier, waited on just before the first
+    // remote store: every CTA of the cluster has started by then (the arrive
+    // carries no ordering; it only says this CTA is running).
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     const int ctas = multi ? clusters * kCluster : kCluster, cta = multi ? cid * kCluster + rank : rank;
     const int chunk = (L + ctas - 1) / ctas;
     const int t0 = min(L, cta * chunk), t1 = min(L, t0 + chunk);
@@ -499,6 +503,7 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     // CTA; after one cluster barrier every rank folds from its own shared
     // memory and no CTA touches another's again.
     __syncthreads();  // this CTA's partial is complete
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every peer is running
     {
         const int q = tid >> 4, c = tid & 15;
         const float *src = c < 4 ? cta_part + 4 * c : cta_part + 2 * kAttnMaxGroup + q * kOutPer + 4 * (c - 4);
