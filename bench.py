@@ -13,13 +13,22 @@ positions 512..767 (each 256-step segment restarts from the post-prompt state).
           pinned host->device copy of the token state, one graph replay and one
           device->host read of the top-2, host synchronised every step.
 
+The default run adds, in the same JSON line, the other configurations the
+metric names, each a sub-object with its own value, e2e, roofline and clocks:
+  bs64          64 independent sessions per GPU (contexts 128..8192), batched
+                tcgen05 decode; at N > 1 weak scaling (64 sessions per GPU);
+  bs64_strong   N > 1 only: 64 sessions in all, dealt over the N GPUs;
+  bf16_ctx4096  BF16 weights, 4096-token prompt, 512-token decode window;
+  bounded       two bounded byte-codec sessions per GPU (below).
+--no-extras skips them; --config runs one configuration alone.
+
 With --config bf16-bounded a step is one token of each of the GPU's bounded
 sessions through ring_push (include/bounded_cache.h), which reads the top-2 back
 every token by design (abort and recovery are decided per token on the host):
 value is CUDA-event time over those steps, e2e the host clock over a second pass.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-       [--config fp32-ctx512 | bf16-ctx4096 | fp32-2layer | bf16-bounded]
+       [--config fp32-ctx512 | bf16-ctx4096 | fp32-2layer | bf16-bounded | bf16-batch64] [--no-extras]
 Under torchrun (N > 1) every rank runs its own replica; rank 0 prints one JSON line.
 """
 from __future__ import annotations
@@ -72,53 +81,85 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (read-only queries)."""
+    """nvidia-smi samples (read-only queries) for the whole run, each stamped by
+    nvidia-smi's own clock; summary(t0, t1) reports the samples that fall in a
+    window of the host clock (widened by `pad` seconds on both sides)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: int):
         self.device = device
         self.proc = None
+        self.lines = []
+        self.reader = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
+
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            if self.reader:
+                self.reader.join(timeout=5)
+            self.proc = None
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
+    @staticmethod
+    def _stamp(text):
+        from datetime import datetime
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                return datetime.strptime(text.strip(), fmt).timestamp()
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
+        return None
+
+    def summary(self, t0=None, t1=None, pad=0.25):
+        sm, mx, reasons, n_all = [], None, set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in list(self.lines):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            when = self._stamp(parts[0])
+            if t0 is not None and (when is None or when < t0 - pad or when > t1 + pad):
+                continue
+            try:
+                sm.append(float(parts[2]))
+                mx = float(parts[3])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[6:10]):
                 if flag.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window_s": None if t0 is None else round(t1 - t0 + 2 * pad, 3)}
+
+
+CLOCKS = None  # the run's sampler (started in main before any GPU work)
+
+
+def clocks_between(t0, t1):
+    return CLOCKS.summary(t0, t1) if CLOCKS else {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
 
 
 def dist_setup(n_gpus: int):
@@ -289,19 +330,20 @@ def run_bounded(args, cfg, world, rank, local, dist, torch):
                 assert g.commit(st["frames"].pop()) == 0
                 counts["commits"] += 1
 
+    t_warm = time.time()
     for _ in range(max(args.warmup, 3)):
         step()
     L.gpu_sync()
     for key in counts:
         counts[key] = 0
     barrier(dist, torch)
-    with ClockSampler(local) as clocks:
-        L.qwen_b200_mark(0)
-        for _ in range(args.steps):
-            step()
-        L.qwen_b200_mark(1)
-        L.gpu_sync()
-        device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    L.qwen_b200_mark(0)
+    for _ in range(args.steps):
+        step()
+    L.qwen_b200_mark(1)
+    L.gpu_sync()
+    device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    clocks = clocks_between(t_warm, time.time())
     timed = dict(counts)
     barrier(dist, torch)
     device_ms = max_over_ranks(device_ms, dist, torch)
@@ -358,7 +400,7 @@ def run_bounded(args, cfg, world, rank, local, dist, torch):
         "ring_attention_ms_layer0": round(ring_ms, 5),
         "ring_state": [{"position": v.cursor, "evictions": v.population, "retained": v.active,
                         "restores": v.restores} for v in views],
-        "clocks": clocks.summary(),
+        "clocks": clocks,
     }
 
 
@@ -373,8 +415,16 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
     model = cm.Model(shape, 2026 + rank, cm.BENCH_LAW, cfg["profile"])
     n, seg = cfg["batch"], cfg["segment"]
     steps = max(seg, (args.steps // seg) * seg)
-    rng = np.random.default_rng(11 + rank)
-    lengths = [int(v) for v in rng.integers(cfg["ctx"][0], cfg["ctx"][1] + 1, n)]
+    strong = bool(cfg.get("strong"))
+    if strong:  # one fixed set of `total` sessions, dealt round-robin over the ranks
+        total = cfg["total"]
+        every = np.random.default_rng(11).integers(cfg["ctx"][0], cfg["ctx"][1] + 1, total)
+        lengths = [int(v) for v in every[rank::world]]
+        n = len(lengths)
+        rng = np.random.default_rng(1011 + rank)
+    else:
+        rng = np.random.default_rng(11 + rank)
+        lengths = [int(v) for v in rng.integers(cfg["ctx"][0], cfg["ctx"][1] + 1, n)]
     sessions = []
     for i, ln in enumerate(lengths):
         s = cm.Session(model, ln + steps // 2 + seg + max(args.warmup, 3) + 2)
@@ -404,15 +454,16 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
             pos = [p + k for p in pos]
             tok = [tops[i].first for i in range(n)]
 
+    t_warm = time.time()
     segment(max(args.warmup, 3), False)
     barrier(dist, torch)
-    with ClockSampler(local) as clocks:
-        L.qwen_b200_mark(0)
-        for c in range(steps // seg):
-            segment(seg, c % 2 == 0)
-        L.qwen_b200_mark(1)
-        L.gpu_sync()
-        device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    L.qwen_b200_mark(0)
+    for c in range(steps // seg):
+        segment(seg, c % 2 == 0)
+    L.qwen_b200_mark(1)
+    L.gpu_sync()
+    device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    clocks = clocks_between(t_warm, time.time())
     barrier(dist, torch)
     device_ms = max_over_ranks(device_ms, dist, torch)
     mean_pos = sum(pos) / n
@@ -459,20 +510,21 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
     for s in sessions:
         s.free()
     model.free()
-    tokens_total = steps * n * world
+    tokens_total = steps * (cfg["total"] if strong else n * world)
     return {
         "metric": METRIC, "value": round(tokens_total / (device_ms * 1e-3), 2), "unit": "tokens/s",
         "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16-weights/f32",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+        "dtype": "bf16-weights/f32", "data": "synthetic",
         "config": {"workload": "qwen2.5-1.5b-bf16-batch64", "layers": shape.layers, "batch": n,
-                   "sessions_total": n * world, "context": "uniform 128..8192 per session (seeded)",
+                   "sessions_total": cfg["total"] if strong else n * world,
+                   "context": "uniform 128..8192 per session (seeded)",
                    "mean_position": round(mean_pos, 1), "segment": seg,
                    "checkpoints": "every segment; rollback after every second segment",
                    "kv_prefill": "context K/V rows are seeded synthetic values; decode steps exact",
                    "parallelism": f"replicas{world}", "weights": "seeded N(0,0.02) random init",
                    "l2": "inputs larger than L2 (weights and K/V stream from HBM every step)"},
-        "e2e": {"value": round(e2e_steps * n * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+        "e2e": {"value": round(e2e_steps * tokens_total / steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * 16},
         "gpu_launches": (shape.layers * 8 + 4) * (steps + max(args.warmup, 3)),
         "roofline": {"bound": "hbm",
@@ -489,7 +541,7 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
         "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
                           "frac": round(step_bytes / (ms_per_step * 1e6) / peak, 4)},
         "stage_ms_layer0": {k: round(v, 5) for k, v in stage.items()},
-        "clocks": clocks.summary(),
+        "clocks": clocks,
     }
 
 
@@ -544,15 +596,16 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
             k -= n
 
     # Warm-up, then exactly K timed chained steps.
+    t_warm = time.time()
     enqueue_steps(max(args.warmup, 3))
     L.gpu_sync()
     barrier(dist, torch)
-    with ClockSampler(local) as clocks:
-        L.qwen_b200_mark(0)
-        enqueue_steps(args.steps)
-        L.qwen_b200_mark(1)
-        L.gpu_sync()
-        device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    L.qwen_b200_mark(0)
+    enqueue_steps(args.steps)
+    L.qwen_b200_mark(1)
+    L.gpu_sync()
+    device_ms = L.qwen_b200_elapsed_ms(0, 1)
+    clocks = clocks_between(t_warm, time.time())
     barrier(dist, torch)
     top = cm.Top2()
     assert L.qwen_b200_last(runner, top) == 0
@@ -620,7 +673,7 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
         "prefill": {"tokens": cfg["prompt"], "ms": round(prefill_ms, 3),
                     "tokens_per_s": round(cfg["prompt"] / (prefill_ms * 1e-3), 1),
                     "path": "batched tensor-core steps of 64 tokens" if es == 2 else "token by token (FP32 weights)"},
-        "clocks": clocks.summary(),
+        "clocks": clocks,
         "last_top2": top.tuple(),
     }
     return line
@@ -632,8 +685,10 @@ def main():
     ap.add_argument("--steps", type=int, default=1024)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="fp32-ctx512")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default=DEFAULT_CONFIG)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default configuration only: skip the batch-64, long-context and bounded sub-lines")
     ap.add_argument("--token-mode", choices=["graph", "persistent"], default="graph",
                     help="batch-1 whole-token execution: the per-stage token graph or the persistent kernel")
     args = ap.parse_args()
@@ -664,41 +719,67 @@ def main():
         return
 
     world, rank, local, dist, torch = dist_setup(args.gpus)
+    global CLOCKS
+    CLOCKS = ClockSampler(local).start()
+    try:
+        line = run_workload(args, args.config, world, rank, local, dist, torch, cpu=not args.no_cpu_baseline)
+        if args.config == DEFAULT_CONFIG and not args.no_extras:
+            # The other configurations the metric names, measured in the same run:
+            # 64-session batched decode (weak scaling: 64 sessions per GPU; at N > 1
+            # also strong scaling: 64 sessions in all), BF16 long context, and the
+            # bounded byte-codec sessions.
+            line["bs64"] = compact(run_workload(args, "bf16-batch64", world, rank, local, dist, torch))
+            if world > 1:
+                strong = dict(CONFIGS["bf16-batch64"], strong=True, total=64)
+                line["bs64_strong"] = compact(run_batched(args, strong, world, rank, local, dist, torch))
+            line["bf16_ctx4096"] = compact(run_workload(args, "bf16-ctx4096", world, rank, local, dist, torch))
+            line["bounded"] = compact(run_workload(args, "bf16-bounded", world, rank, local, dist, torch))
+    finally:
+        CLOCKS.stop()
+    if rank == 0:
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+DEFAULT_CONFIG = "fp32-ctx512"
+
+
+def compact(line):
+    """A workload's line as a sub-object of the headline line."""
+    return {k: v for k, v in line.items() if k not in ("metric", "higher_is_better", "vs_baseline", "data")}
+
+
+def run_workload(args, name, world, rank, local, dist, torch, cpu=False):
+    """One configuration's line; with cpu, rank 0 of a 1-GPU run adds the
+    reference CPU path timed on the host cores."""
+    cfg = CONFIGS[name]
+    sub = argparse.Namespace(**vars(args))
+    sub.config = name
     if "batch" in cfg:
-        line = run_batched(args, cfg, world, rank, local, dist, torch)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line = run_batched(sub, cfg, world, rank, local, dist, torch)
+        if cpu and rank == 0 and world == 1:
             rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], True)
             line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                                     "sample": sample + "; at these sessions' contexts the reference's attention adds "
                                               "about a quarter to each token's arithmetic"}
-        if rank == 0:
-            print(json.dumps(line))
-        if dist:
-            dist.destroy_process_group()
-        return
+        return line
     if "ring" in cfg:
-        line = run_bounded(args, cfg, world, rank, local, dist, torch)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line = run_bounded(sub, cfg, world, rank, local, dist, torch)
+        if cpu and rank == 0 and world == 1:
             got = cpu_reference_ring_rate(cfg)
             if got:
                 rate, cores, sample, kind = got
                 line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                                         "sample": sample}
-        if rank == 0:
-            print(json.dumps(line))
-        if dist:
-            dist.destroy_process_group()
-        return
-    line = run_b200(args, cfg, world, rank, local, dist, torch)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        return line
+    line = run_b200(sub, cfg, world, rank, local, dist, torch)
+    if cpu and rank == 0 and world == 1:
         rate, cores, sample, kind, ref_logits = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
         line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                                 "sample": sample}
         line["max_abs_dlogit"] = gpu_dlogit(cfg["layers"], cfg["profile"], ref_logits)
-    if rank == 0:
-        print(json.dumps(line))
-    if dist:
-        dist.destroy_process_group()
+    return line
 
 
 if __name__ == "__main__":

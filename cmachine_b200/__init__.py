@@ -353,6 +353,20 @@ class Session:
                 self.L.gpu_read(ptr(out[h]), c_void_p(base + h * v.capacity * s.head * 4), v.position * s.head * 4)
         return out
 
+    def write_kv(self, layer: int, kind: int, rows: np.ndarray):
+        """Write K (kind 0) or V (kind 1) rows 0..n-1 of a dense layer from [kvheads][n][head]."""
+        v, s = self.view(), self.model.shape
+        rows = np.ascontiguousarray(rows, np.float32)
+        n = rows.shape[1]
+        assert n <= v.capacity
+        base = (v.values if kind else v.keys) + layer * s.kvheads * v.capacity * s.head * 4
+        for h in range(s.kvheads):
+            self.L.gpu_write(c_void_p(base + h * v.capacity * s.head * 4), ptr(rows[h]), n * s.head * 4)
+
+    def set_cursor(self, position: int, pending: int) -> int:
+        """Place the cursor after `position` cached rows written by write_kv (qwen_b200_session_set_cursor)."""
+        return self.L.qwen_b200_session_set_cursor(self.handle, position, pending)
+
     def kv_rows(self):
         """This token's K and V rows of the last layer computed: ([kvheads * head], [kvheads * head])."""
         v, s = self.view(), self.model.shape

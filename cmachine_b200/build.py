@@ -83,10 +83,15 @@ def build_library(verbose: bool = False) -> Path:
 
 def build_oracle(verbose: bool = False) -> None:
     """The CPU checkers (test infrastructure): the oracle always, and the
-    reference builds when the reference sources are present."""
-    _run(["make", "-s", "-C", str(ROOT / "oracle"), "liboracle.so"])
-    if Path("/root/reference/src/qwen.c").exists():
-        _run(["make", "-s", "-C", str(ROOT / "oracle"), "ref"])
+    reference builds when the reference sources are present. The reference
+    location is oracle/Makefile's REF, overridden by the CMACHINE_REFERENCE
+    environment variable."""
+    make = ["make", "-s", "-C", str(ROOT / "oracle")]
+    ref = os.environ.get("CMACHINE_REFERENCE")
+    if ref:
+        make.append(f"REF={ref}")
+    _run(make + ["liboracle.so"])
+    _run(make + ["ref-if-present"])
     if verbose:
         print("oracle built")
 

@@ -1324,8 +1324,8 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
     if (!d || decoder_view(d, &s, &layers, &embed, &norm, &den, &dtype) || dtype != 2 || s.hidden != kHd ||
         s.intermediate != kFf || s.qheads != 12 || s.kvheads != 2 || s.head != 128 || s.vocab % 128)
         return nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
+    static PerDeviceOnce once;
+    once.run([] {
         gemm_setup<EpiQkv>();
         gemm_setup<EpiResid>();
         gemm_setup<EpiSwiglu>();

@@ -4,6 +4,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <mutex>
 
 // The reference treats every CUDA error as fatal: message on stderr, exit(2)
 // (src/qwen_cuda.cu:8). The primitive ABI keeps that contract.
@@ -23,6 +24,24 @@
     } while (0)
 
 namespace tcm {
+
+// Runs a set-up step once on every device this process uses. Function
+// attributes such as the dynamic shared-memory limit belong to the device
+// context, so a process that drives several GPUs must set them on each.
+struct PerDeviceOnce {
+    std::mutex lock;
+    bool done[64] = {};
+    template <typename Fn> void run(Fn fn) {
+        int dev = 0;
+        TCM_CUDA(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= 64) TCM_FATAL("device index %d out of range", dev);
+        std::lock_guard<std::mutex> hold(lock);
+        if (!done[dev]) {
+            fn();
+            done[dev] = true;
+        }
+    }
+};
 
 // The library's stream. It is created with default (blocking) flags, so work
 // on it is ordered with the legacy default stream that reference-style callers

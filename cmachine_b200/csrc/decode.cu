@@ -690,8 +690,8 @@ template <typename WT> void setup_kernels_typed() {
     set_smem(readout_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
 }
 void setup_kernels() {
-    static std::once_flag once;
-    std::call_once(once, [] {
+    static PerDeviceOnce once;
+    once.run([] {
         setup_kernels_typed<float>();
         setup_kernels_typed<uint16_t>();
         setup_attention();

@@ -825,13 +825,15 @@ template <typename WT> int setup_typed() {
 }  // namespace
 
 int persistent_blocks_per_sm(int dtype) {
-    static std::once_flag once;
-    static int fits[2];
-    std::call_once(once, [] {
-        fits[0] = setup_typed<float>();
-        fits[1] = setup_typed<uint16_t>();
+    static PerDeviceOnce once;
+    static int fits[64][2];
+    int dev = 0;
+    TCM_CUDA(cudaGetDevice(&dev));
+    once.run([dev] {
+        fits[dev][0] = setup_typed<float>();
+        fits[dev][1] = setup_typed<uint16_t>();
     });
-    return fits[dtype == 2 ? 1 : 0];
+    return fits[dev][dtype == 2 ? 1 : 0];
 }
 
 void launch_persistent(int dtype, const PersistArgs &a, int grid, cudaStream_t stream) {

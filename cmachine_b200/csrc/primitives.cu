@@ -87,8 +87,8 @@ static void matvec_typed(const WT *w, int in, int out, const float *x, float *y,
     if (!aligned) {
         matvec_scalar_kernel<WT><<<blocks, kThreads, 0, s>>>(w, in, out, x, y);
     } else if ((size_t)in * 4 <= 96 * 1024) {
-        static std::once_flag once;
-        std::call_once(once, [] {
+        static PerDeviceOnce once;
+        once.run([] {
             TCM_CUDA(cudaFuncSetAttribute(matvec_kernel<WT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           96 * 1024));
         });
@@ -332,8 +332,8 @@ void attention_generic(float *out, const float *q, const float *keys, const floa
 void attention_split(const float *q, const AttnSource &source, bool bytes, int capacity, int length,
                      const int *position, int qheads, int kvheads, int nsplit, float *part, unsigned *counters,
                      float *out, cudaStream_t s, bool pdl) {
-    static std::once_flag once;
-    std::call_once(once, [] {
+    static PerDeviceOnce once;
+    once.run([] {
         TCM_CUDA(cudaFuncSetAttribute(attn_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kAttnSmemBytes));
         TCM_CUDA(cudaFuncSetAttribute(attn_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -81,10 +81,13 @@ void gpu_attention(TcmGpu *, float *out, const float *q, const float *keys, cons
  * Its split-K scratch is a fixed 1.2 MB device array inside the library, held
  * by every GPU that loads it: limits are dim == 128, 1 <= kvheads <= 4, at most
  * 8 query heads per KV head, 1 <= length <= capacity; other sizes return -1
- * with a message on stderr and launch nothing. Returns 0 when launched. The
- * first call on each device looks up the array's device address, so make it
- * before any stream capture. Calls share the array: calls that overlap on the
- * GPU race. */
+ * with a message on stderr and launch nothing. Returns 0 when launched. CUDA
+ * errors are fatal (message, exit(2)) as everywhere in this ABI; only sizes and
+ * alignment come back as -1. The first call on each device looks up the
+ * array's device address, and under the runtime's lazy module loading that is
+ * also when the device first holds the array's 1.2 MB: make that first call at
+ * start-up, before handing device memory to a pool and before any stream
+ * capture. Calls share the array: calls that overlap on the GPU race. */
 int gpu_attention_static(float *out, const float *q, const float *keys, const float *values, int qheads,
                          int kvheads, int dim, int capacity, int length);
 /* gate = silu(gate) * up. (src/gpu.h:35) */

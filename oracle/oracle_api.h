@@ -37,6 +37,13 @@ int orc_position(void *session);
 void orc_read_kv(void *session, int layer, int kind, float *out);
 /* The final-norm input x of the last pushed token (hidden floats). */
 void orc_read_hidden(void *session, float *out);
+/* Context injection for long-context parity: write K (kind 0) or V (kind 1)
+ * rows 0..rows-1 of one layer from in[kvheads][rows][head], and place the
+ * cursor after `position` cached rows (the next push appends row `position`).
+ * Both checkers accept the same calls, so seeded contexts of any length can be
+ * compared without prefilling them token by token. */
+void orc_write_kv(void *session, int layer, int kind, int rows, const float *in);
+int orc_set_cursor(void *session, int position);
 /* Bounded byte-codec ring sessions (liboracle.so only). */
 typedef struct {
     int cursor;

@@ -425,3 +425,18 @@ void orc_read_hidden(void *p, float *out) {
     OrcSession *s = p;
     memcpy(out, s->x, (size_t)s->model->shape.hidden * 4);
 }
+
+void orc_write_kv(void *p, int layer, int kind, int rows, const float *in) {
+    OrcSession *s = p;
+    const OrcShape *S = &s->model->shape;
+    float *dst = (kind ? s->values : s->keys) + (size_t)layer * S->kvheads * s->capacity * S->head;
+    for (int h = 0; h < S->kvheads; h++)
+        memcpy(dst + (size_t)h * s->capacity * S->head, in + (size_t)h * rows * S->head, (size_t)rows * S->head * 4);
+}
+
+int orc_set_cursor(void *p, int position) {
+    OrcSession *s = p;
+    if (s->ring || position < 0 || position >= s->capacity) return -1;
+    s->position = position;
+    return 0;
+}

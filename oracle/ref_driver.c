@@ -138,3 +138,25 @@ void orc_read_hidden(void *p, float *out) {
     QwenSession *s = p;
     gpu_read(out, s->x, (size_t)s->model->hidden * 4);
 }
+
+void orc_write_kv(void *p, int layer, int kind, int rows, const float *in) {
+    QwenSession *s = p;
+    const QwenModel *m = s->model;
+    float *dst = (kind ? s->values : s->keys) + (size_t)layer * m->kvheads * s->capacity * m->head;
+    for (int h = 0; h < m->kvheads; h++)
+        gpu_write(dst + (size_t)h * s->capacity * m->head, in + (size_t)h * rows * m->head, (size_t)rows * m->head * 4);
+}
+
+/* The reference keeps the cursor in QwenSession.position (src/qwen.h:72);
+ * qwen_begin_token appends the next row there. */
+int orc_set_cursor(void *p, int position) {
+    QwenSession *s = p;
+    if (s->phase == 2 || s->depth || position < 0 || position >= s->capacity) return -1;
+    s->position = position;
+    return 0;
+}
+
+/* The reference's nested stack (src/qwen.c:416-431), for replay checks of the
+ * reference host over the B200 primitives. */
+int orc_stack_push(void *p, uint64_t *id) { return qwen_stack_push((QwenSession *)p, id); }
+int orc_stack_rollback(void *p, uint64_t id) { return qwen_stack_rollback((QwenSession *)p, id); }

@@ -37,6 +37,11 @@ def load(path: Path):
     L.orc_read_hidden.argtypes = [c_void_p, c_void_p]
     L.orc_weight_value.restype = c_float
     L.orc_weight_value.argtypes = [c_void_p, c_uint32, c_uint64]
+    L.orc_write_kv.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p]
+    L.orc_set_cursor.argtypes = [c_void_p, c_int]
+    if hasattr(L, "orc_stack_push"):  # the reference drivers only
+        L.orc_stack_push.argtypes = [c_void_p, POINTER(c_uint64)]
+        L.orc_stack_rollback.argtypes = [c_void_p, c_uint64]
     return L
 
 
@@ -65,6 +70,14 @@ class CpuDecoder:
         out = np.empty((self.shape.kvheads, pos, self.shape.head), np.float32)
         self.L.orc_read_kv(self.session, layer, kind, c_void_p(out.ctypes.data))
         return out
+
+    def write_kv(self, layer: int, kind: int, rows: np.ndarray):
+        """K (kind 0) or V (kind 1) rows 0..n-1 of one layer from [kvheads][n][head]."""
+        rows = np.ascontiguousarray(rows, np.float32)
+        self.L.orc_write_kv(self.session, layer, kind, rows.shape[1], c_void_p(rows.ctypes.data))
+
+    def set_cursor(self, position: int):
+        assert self.L.orc_set_cursor(self.session, position) == 0
 
     def hidden(self) -> np.ndarray:
         out = np.empty(self.shape.hidden, np.float32)
@@ -122,3 +135,20 @@ def codec_rows(x: np.ndarray):
         assert L.orc_codec(c_void_p(x[i].ctypes.data), c_void_p(codes[i].ctypes.data),
                            c_void_p(scales[i:].ctypes.data)) == 0
     return codes, scales
+
+
+def seeded_context(shape, seed: int, rows: int, scale: float = 0.8):
+    """Synthetic cached K/V rows for long-context parity: per layer and kind an
+    array [kvheads][rows][head] of N(0, scale) values (scale 0.8 is the spread of
+    the decoder's own K/V rows under N(0, 0.02) weights), plus every 97th row
+    scaled up 4x so the softmax has sharp peaks to place exactly."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(shape.layers):
+        pair = []
+        for _ in range(2):
+            a = rng.standard_normal((shape.kvheads, rows, shape.head), dtype=np.float32) * np.float32(scale)
+            a[:, ::97, :] *= np.float32(4.0)
+            pair.append(a)
+        out.append(pair)
+    return out

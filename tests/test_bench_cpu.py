@@ -50,3 +50,21 @@ def test_reference_arm_line():
     assert line["impl"] == "reference" and line["unit"] == "tokens/s" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference"
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_clock_sampler_window():
+    """The run-long sampler keeps only samples stamped inside the asked window
+    and reports slowdown reasons seen there."""
+    from datetime import datetime
+    c = bench.ClockSampler(0)
+    t = datetime(2026, 1, 2, 3, 4, 5).timestamp()
+
+    def row(dt, mhz, thermal="Not Active"):
+        stamp = datetime.fromtimestamp(t + dt).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+        return f"{stamp}, 0, {mhz}, 1965, 700.0, 0x0, Not Active, {thermal}, Not Active, Not Active\n"
+
+    c.lines = [row(-5, 900), row(0.1, 1965), row(0.3, 1950), row(0.5, 1965, "Active"), row(9, 800)]
+    got = c.summary(t, t + 0.5, pad=0.05)
+    assert got["samples"] == 3 and got["sm_mhz"] == 1965 and got["sm_max_mhz"] == 1965
+    assert got["reasons"] == ["hw_thermal_slowdown"]
+    assert c.summary()["samples"] == 5

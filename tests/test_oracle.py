@@ -75,6 +75,44 @@ def test_oracle_bit_exact_with_reference_build(bf16, shape_kind):
         b.close()
 
 
+@pytest.mark.skipif(not REF_CPU.exists(), reason="reference sources not built here")
+@pytest.mark.parametrize("bf16", [False, True])
+def test_oracle_bit_exact_with_reference_on_injected_context(bf16):
+    """Long-context pin: both checkers get the same 1,500 seeded K/V rows per
+    layer through orc_write_kv / orc_set_cursor, then decode 6 tokens. The
+    oracle's attention (and everything after it) must equal the reference's
+    CPU path bit for bit at that length, which is what the GPU long-context
+    parity tests lean on."""
+    from checkers import seeded_context
+    shape = small_shape(2, 8192, 1536, (12, 2), 1024)
+    shape.max_position = 2048
+    rows, seed = 1500, 314 + int(bf16)
+    a = CpuDecoder(ORACLE, shape, seed, cm.TEST_LAW, bf16, rows + 8)
+    b = CpuDecoder(REF_CPU, shape, seed, cm.TEST_LAW, bf16, rows + 8)
+    try:
+        for layer, pair in enumerate(seeded_context(shape, seed, rows)):
+            for kind in (0, 1):
+                a.write_kv(layer, kind, pair[kind])
+                b.write_kv(layer, kind, pair[kind])
+        a.set_cursor(rows)
+        b.set_cursor(rows)
+        token = 4321
+        for _ in range(6):
+            ta, la = a.push(token)
+            tb, lb = b.push(token)
+            assert ta == tb
+            assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+            token = ta[0]
+        for layer in range(shape.layers):
+            for kind in (0, 1):
+                ka, kb = a.kv(layer, kind), b.kv(layer, kind)
+                assert ka.shape[1] == rows + 6
+                assert np.array_equal(ka.view(np.uint32), kb.view(np.uint32))
+    finally:
+        a.close()
+        b.close()
+
+
 # ---------------------------------------------------------------- seeded generator
 M64 = (1 << 64) - 1
 
