@@ -19,6 +19,8 @@ metric names, each a sub-object with its own value, e2e, roofline and clocks:
                 tcgen05 decode; at N > 1 weak scaling (64 sessions per GPU);
   bs64_strong   N > 1 only: 64 sessions in all, dealt over the N GPUs;
   bf16_ctx4096  BF16 weights, 4096-token prompt, 512-token decode window;
+  bf16_ctx4096_tp  N > 1 only: the same single session split over the N GPUs
+                (tensor-parallel MLP and readout; value = that session's tokens/s);
   bounded       two bounded byte-codec sessions per GPU (below).
 --no-extras skips them; --config runs one configuration alone.
 
@@ -565,22 +567,31 @@ def gpu_dlogit(layers: int, profile: int, ref_logits):
 
 
 # ---------------------------------------------------------------- B200 arm
-def run_b200(args, cfg, world, rank, local, dist, torch):
+def run_b200(args, cfg, world, rank, local, dist, torch, tp=False):
+    """Batch-1 decode: one independent session per GPU, or with tp one session
+    split over all the GPUs (tensor-parallel MLP and readout)."""
     import cmachine_b200 as cm
     L = cm.lib()
     L.qwen_b200_set_device(local)
     shape = cm.qwen_shape(cfg["layers"], 32768)
-    model = cm.Model(shape, 2026 + rank, cm.BENCH_LAW, cfg["profile"])
+    salt = 0 if tp else rank  # a tensor-parallel group decodes one model and one prompt
+    model = cm.Model(shape, 2026 + salt, cm.BENCH_LAW, cfg["profile"])
     capacity = cfg["prompt"] + cfg["window"] + 1
     s = cm.Session(model, capacity)
+    if tp:
+        status, handle = s.tp_open(rank, world)
+        assert status == 0
+        assert s.tp_connect(cm.tp_gather(dist, handle)) == 0
     # The prompt through qwen_prefill (batched causal tensor-core steps on a BF16
     # model; token by token on FP32), timed on the device.
     L.gpu_sync()
+    barrier(dist, torch)
     L.qwen_b200_mark(4)
-    assert s.prefill(prompt_tokens(7 + rank, cfg["prompt"], shape.vocab)) == 0
+    assert s.prefill(prompt_tokens(7 + salt, cfg["prompt"], shape.vocab)) == 0
     L.qwen_b200_mark(5)
     L.gpu_sync()
     prefill_ms = L.qwen_b200_elapsed_ms(4, 5)
+    barrier(dist, torch)
     status, ckpt = s.checkpoint()
     assert status == 0
     p0, pos0, window = s.pending, s.position, cfg["window"]
@@ -630,19 +641,29 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
     e2e_ms = max_over_ranks(L.qwen_b200_elapsed_ms(2, 3), dist, torch)
     barrier(dist, torch)
 
-    # Roofline of the dominant kernel: the fused gate/up GEMV (half the bytes).
+    # Roofline of the dominant kernel: the fused gate/up GEMV (half the bytes;
+    # with tp this rank's 1/world of its rows).
     es = 2 if cfg["profile"] == 2 else 4
+    share = world if tp else 1
     gateup_ms = L.qwen_b200_time_stage(runner, 3, 0, pos0, 30)
-    gateup_bytes = 2 * shape.intermediate * shape.hidden * es + shape.intermediate * 4
+    gateup_bytes = (2 * shape.intermediate * shape.hidden * es + shape.intermediate * 4) // share
     peak, peak_kind = measured_peaks()
     achieved = gateup_bytes / (gateup_ms * 1e-3) / 1e9
     weight_bytes = model.weight_bytes
+    if tp:  # per GPU: the MLP matrices and the readout rows are split, the rest replicated
+        split = (3 * shape.intermediate * shape.hidden * shape.layers + shape.vocab * shape.hidden) * es
+        weight_bytes = weight_bytes - split + split // world
     mean_ctx = pos0 + window / 2
     kv_bytes = 2 * shape.layers * shape.kvheads * shape.head * 4 * mean_ctx
     step_bytes = weight_bytes + kv_bytes
     ms_per_step = device_ms / args.steps
     stage_names = ["qkv", "attention", "oproj", "gateup", "down", "readout"]
-    stage_ms = {name: round(L.qwen_b200_time_stage(runner, i, 0, pos0, 10), 5) for i, name in enumerate(stage_names)}
+    stage_ms = {name: round(L.qwen_b200_time_stage(runner, i, 0, pos0, 10), 5) for i, name in enumerate(stage_names)
+                if not (tp and i >= 4)}  # the group's exchange stages run only as whole tokens
+    barrier(dist, torch)
+    if tp:
+        assert s.tp_close() == 0
+        barrier(dist, torch)
     s.free()
     model.free()
     traffic = None
@@ -650,16 +671,19 @@ def run_b200(args, cfg, world, rank, local, dist, torch):
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"gateup_{'bf16' if es == 2 else 'fp32'}")
 
+    sessions = 1 if tp else world
     line = {
-        "metric": METRIC, "value": round(args.steps * world / (device_ms * 1e-3), 2), "unit": "tokens/s",
+        "metric": METRIC, "value": round(args.steps * sessions / (device_ms * 1e-3), 2), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "strong" if tp else "weak",
         "vs_baseline": None, "dtype": "bf16-weights/f32" if es == 2 else "f32", "data": "synthetic",
         "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": shape.layers, "batch": 1,
                    "prompt_tokens": cfg["prompt"], "decode_window": window, "token_execution": args.token_mode,
-                   "weights": "seeded N(0,0.02) random init", "parallelism": f"replicas{world}",
+                   "weights": "seeded N(0,0.02) random init",
+                   "parallelism": f"tensor{world} (MLP units and readout rows split, peer-memory exchange)" if tp
+                   else f"replicas{world}",
                    "l2": "inputs larger than L2 (weights stream from HBM every step)"},
-        "e2e": {"value": round(args.steps * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+        "e2e": {"value": round(args.steps * sessions / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 32},
         "gpu_launches": per_token_launches * args.steps + (args.steps + window - 1) // window,
         "roofline": {"bound": "hbm", "kernel": "gateup_kernel (RMSNorm + gate/up GEMV + SwiGLU)",
@@ -733,6 +757,11 @@ def main():
                 strong = dict(CONFIGS["bf16-batch64"], strong=True, total=64)
                 line["bs64_strong"] = compact(run_batched(args, strong, world, rank, local, dist, torch))
             line["bf16_ctx4096"] = compact(run_workload(args, "bf16-ctx4096", world, rank, local, dist, torch))
+            if world > 1 and world in (2, 4, 8):
+                sub = argparse.Namespace(**vars(args))
+                sub.config = "bf16-ctx4096"
+                line["bf16_ctx4096_tp"] = compact(run_b200(sub, CONFIGS["bf16-ctx4096"], world, rank, local, dist,
+                                                           torch, tp=True))
             line["bounded"] = compact(run_workload(args, "bf16-bounded", world, rank, local, dist, torch))
     finally:
         CLOCKS.stop()

@@ -81,6 +81,24 @@ PORT_NAMES = ["input", "query", "key", "value", "attention", "mlp_input", "mlp_g
               "output", "attention_write", "raw_receiver", "consumed_attention_write", "consumed_mlp_write"]
 
 _LIB = None
+TP_HANDLE_BYTES = 256  # QWEN_B200_TP_HANDLE_BYTES (include/qwen_b200.h)
+
+
+def tp_gather(dist, handle: bytes) -> bytes:
+    """Every rank's tensor-parallel handle, concatenated in rank order, over a
+    torch.distributed process group of any backend (the handles are small
+    host byte strings)."""
+    assert len(handle) == TP_HANDLE_BYTES
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, handle)
+    assert all(isinstance(h, bytes) and len(h) == TP_HANDLE_BYTES for h in out)
+    return b"".join(out)
+
+
+def tp_shares(total: int, world: int):
+    """[begin, end) of each rank's share of `total` rows, as the kernels split
+    the vocabulary (floor(rank * total / world))."""
+    return [(r * total // world, (r + 1) * total // world) for r in range(world)]
 
 
 def _declare(L, strict: bool = True):
@@ -166,6 +184,8 @@ def _declare(L, strict: bool = True):
         "qwen_b200_batch_cluster_capacity": (c_int, [c_int]),
         "qwen_b200_batch_clusters": (c_int, [P, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
         "qwen_b200_session_set_cursor": (c_int, [P, c_int, c_int]),
+        "qwen_session_tp_open": (c_int, [P, c_int, c_int, P]), "qwen_session_tp_connect": (c_int, [P, P]),
+        "qwen_session_tp_close": (c_int, [P]), "qwen_b200_tp_world": (c_int, [P]),
         "qwen_b200_unregister_matrix": (None, [P]),
         # host/session_view.c
         "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),
@@ -376,6 +396,23 @@ class Session:
         return k, vv
 
     def complete_token(self) -> int: return self.L.qwen_complete_token(self.handle)
+
+    # -- tensor-parallel decode over several GPUs (one process per GPU)
+    def tp_open(self, rank: int, world: int):
+        """qwen_session_tp_open: (status, this rank's handle bytes)."""
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        status = self.L.qwen_session_tp_open(self.handle, rank, world, ctypes.cast(buf, c_void_p))
+        return status, buf.raw
+
+    def tp_connect(self, handles: bytes) -> int:
+        """qwen_session_tp_connect with every rank's handle, in rank order."""
+        buf = ctypes.create_string_buffer(handles, len(handles))
+        return self.L.qwen_session_tp_connect(self.handle, ctypes.cast(buf, c_void_p))
+
+    def tp_close(self) -> int: return self.L.qwen_session_tp_close(self.handle)
+
+    @property
+    def tp_world(self) -> int: return self.L.qwen_b200_tp_world(self.runner)
 
     @property
     def runner(self): return self.L.qwen_b200_session_runner(self.handle)

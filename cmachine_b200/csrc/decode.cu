@@ -16,6 +16,7 @@
 #include "stream.cuh"
 #include "lanes.cuh"
 #include "persistent.cuh"
+#include "tp.cuh"
 #include "kernels.h"
 #include "../../include/qwen_b200.h"
 #include "../../include/tcm_seeded.h"
@@ -272,13 +273,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
 
 // ---------------------------------------------------------------- stage 4: gate/up + SwiGLU
 struct GateUpArgs {
-    const void *wg, *wu;
+    const void *wg, *wu;        // this rank's first gate and up rows
     const float *norm, *x;
     float *h;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
     unsigned *sched;            // row-group counter of this launch site
     float eps;
+    int inter;                  // intermediate units of this rank (all 8960 on one GPU)
 };
 // Items alternate gate row j, up row j; the epilogue forms h_j = silu(g) * u
 // as g / (1 + exp(-g)) * u (src/qwen_cuda.cu:79).
@@ -290,7 +292,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     __shared__ __align__(16) float nw_s[kHidden], x_s[kHidden];
     __shared__ int fail_s, hdr_s[kStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int items = 2 * kInter;
+    const int items = 2 * a.inter;
     const WT *wg = (const WT *)a.wg, *wu = (const WT *)a.wu;
     if (threadIdx.x == 0) fail_s = 0;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
@@ -342,34 +344,52 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
 
 // ---------------------------------------------------------------- stage 5: down projection + residual
 struct DownArgs {
-    const void *w;
-    const float *h;
+    const void *w;              // this rank's first column of the down matrix (row stride 8960)
+    const float *h;             // this rank's intermediate units
     float *x;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
+    TpLink tp;                  // world 1: the sums go straight into the residual
+    int layer;
 };
-// A stage holds RD rows of 8960; 8 / RD warps split each row into contiguous
-// pieces of 280 vectors; the pieces are summed in order into the residual.
-template <typename WT>
+// Row geometry of the down projection when a rank reads F = 8960 / SH columns
+// of every row: RD rows of F per stage (the stage stays ~35 KB); with fewer
+// than eight rows a stage, PIECES warps split each row into contiguous pieces;
+// with more, each warp takes RPW whole rows.
+template <typename WT, int SH> struct DownGeo {
+    static constexpr int E = Geo<WT>::E;
+    static constexpr int F = kInter / SH;
+    static constexpr int RD = Geo<WT>::RD * SH;
+    static constexpr int PIECES = RD >= kConsumerWarps ? 1 : kConsumerWarps / RD;
+    static constexpr int RPW = RD >= kConsumerWarps ? RD / kConsumerWarps : 1;
+    static constexpr int NVP = F / E / PIECES;  // vectors per piece
+    static constexpr int KV = (NVP + 31) / 32;  // per lane
+    static constexpr uint32_t kRowBytes = F * sizeof(WT);
+    static constexpr uint32_t kStageBytes = RD * kRowBytes;
+    static_assert(F % (E * PIECES) == 0 && kRowBytes % 16 == 0, "down row pieces must be whole 16-byte vectors");
+    static_assert(PIECES * RD == kConsumerWarps || RPW * kConsumerWarps == RD, "warps must tile a stage");
+};
+// The pieces of a row are summed in order into the residual row (one GPU), or
+// into the rank's partial of that row, which the group then exchanges.
+template <typename WT, int SH>
 __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    constexpr int RD = Geo<WT>::RD, E = Geo<WT>::E, PIECES = kConsumerWarps / RD;
-    constexpr int NVP = kInter / E / PIECES;  // vectors per piece (280)
-    constexpr int KV = (NVP + 31) / 32;       // per lane (9)
+    using G = DownGeo<WT, SH>;
+    constexpr int RD = G::RD, E = G::E, PIECES = G::PIECES, RPW = G::RPW, NVP = G::NVP, KV = G::KV;
     __shared__ float part_s[2][RD][PIECES];
     __shared__ int fail_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int slot = warp / PIECES, piece = warp % PIECES;
+    const int piece = PIECES > 1 ? warp % PIECES : 0;
     const int r0 = share_begin(kHidden, blockIdx.x, gridDim.x), r1 = share_begin(kHidden, blockIdx.x + 1, gridDim.x);
     const int items = r1 - r0;
     const WT *w = (const WT *)a.w;
     if (threadIdx.x == 0) fail_s = 0;
-    const Ring ring = ring_setup(smem, kDownStages, kDownStage<WT>);
+    const Ring ring = ring_setup(smem, kDownStages, G::kStageBytes);
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
         if (lane == 0)
-            ring_produce(ring, items, RD, kDownRow<WT>, [&](int i) { return (const void *)(w + (size_t)(r0 + i) * kInter); },
+            ring_produce(ring, items, RD, G::kRowBytes, [&](int i) { return (const void *)(w + (size_t)(r0 + i) * kInter); },
                          &a.st->fault);
         return;
     }
@@ -390,18 +410,23 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
         }
     }
     trace_mark(a.trace, 2);
+    constexpr bool group = SH > 1;  // a rank reads part of each row only inside a group
     const int groups = (items + RD - 1) / RD;
     for (int g = 0; g < groups; g++) {
         const int n = min(RD, items - g * RD);
         if (ring_acquire(ring, g, &a.st->fault)) {
-            if (slot < n) {
-                const uint4 *row = reinterpret_cast<const uint4 *>(ring.stage(g % kDownStages) + (size_t)slot * kDownRow<WT>);
-                float acc = 0.f;
 #pragma unroll
-                for (int k = 0; k < KV; k++)
-                    if (lane + 32 * k < NVP) acc = dot_vec(row[piece * NVP + lane + 32 * k], &hr[E * k], acc, WT());
-                acc = warp_sum(acc);
-                if (lane == 0) part_s[g & 1][slot][piece] = acc;
+            for (int j = 0; j < RPW; j++) {
+                const int slot = PIECES > 1 ? warp / PIECES : warp + kConsumerWarps * j;
+                if (slot < n) {
+                    const uint4 *row = reinterpret_cast<const uint4 *>(ring.stage(g % kDownStages) + (size_t)slot * G::kRowBytes);
+                    float acc = 0.f;
+#pragma unroll
+                    for (int k = 0; k < KV; k++)
+                        if (lane + 32 * k < NVP) acc = dot_vec(row[piece * NVP + lane + 32 * k], &hr[E * k], acc, WT());
+                    acc = warp_sum(acc);
+                    if (lane == 0) part_s[g & 1][slot][piece] = acc;
+                }
             }
         } else {
             fail_s = 1;
@@ -414,7 +439,34 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
             float sum = part_s[g & 1][s][0];
 #pragma unroll
             for (int p = 1; p < PIECES; p++) sum = __fadd_rn(sum, part_s[g & 1][s][p]);
-            a.x[row] = __fadd_rn(a.x[row], sum);
+            if (group) {
+                const size_t at = ((size_t)a.layer * a.tp.world + a.tp.rank) * kHidden + row;
+                for (int p = 0; p < a.tp.world; p++) a.tp.part[p][at] = sum;  // peer stores over NVLink
+            } else {
+                a.x[row] = __fadd_rn(a.x[row], sum);
+            }
+        }
+    }
+    if (group && !fail_s) {
+        // This CTA's partial rows are in every rank's area: raise its flag at
+        // each rank, wait for the same CTA of every rank, then add the world
+        // partials of these rows in rank order.
+        __threadfence_system();
+        consumers_sync();
+        const unsigned token = __ldcg(a.tp.epoch) + 1u;
+        const size_t fslot = ((size_t)a.layer * gridDim.x + blockIdx.x) * a.tp.world;
+        if ((int)threadIdx.x < a.tp.world) {
+            st_release_sys(a.tp.flag[threadIdx.x] + fslot + a.tp.rank, token);
+            if (!wait_flag(a.tp.flag[a.tp.rank] + fslot + threadIdx.x, token, &a.st->fault)) fail_s = 1;
+        }
+        consumers_sync();
+        if (!fail_s) {
+            const float *mine = a.tp.part[a.tp.rank] + (size_t)a.layer * a.tp.world * kHidden;
+            for (int row = r0 + (int)threadIdx.x; row < r1; row += kConsumerWarps * 32) {
+                float sum = __ldcv(mine + row);
+                for (int p = 1; p < a.tp.world; p++) sum = __fadd_rn(sum, __ldcv(mine + (size_t)p * kHidden + row));
+                a.x[row] = __fadd_rn(a.x[row], sum);
+            }
         }
     }
     trace_mark(a.trace, 3);
@@ -434,6 +486,7 @@ struct ReadoutArgs {
     unsigned *sched;            // row-group counter of this launch site
     int vocab;
     float eps;
+    TpLink tp;                  // world > 1: this rank's vocabulary rows, logits to every rank, top-2 exchange
 };
 template <typename WT>
 __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs a) {
@@ -444,8 +497,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     __shared__ __align__(16) float nw_s[kHidden], x_s[kHidden];
     __shared__ int last, hdr_s[kStages];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int items = a.vocab;
-    const WT *e = (const WT *)a.embed;
+    const bool group = a.tp.world > 1;
+    const int base = group ? a.tp.vocab_begin : 0;
+    const int items = group ? a.tp.vocab_end - a.tp.vocab_begin : a.vocab;
+    const WT *e = (const WT *)a.embed + (size_t)base * kHidden;
     const Ring ring = ring_setup(smem, kStages, kStage<WT>);
     trace_mark(a.trace, 0);
     pdl_trigger();
@@ -476,9 +531,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
         for (int m = 0; m < R / kConsumerWarps; m++) {
             const int j = warp + kConsumerWarps * m;
             if (j < n) {
-                const int row = grp * R + j;
+                const int row = base + grp * R + j;
                 const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
-                if (lane == 0) a.logits[row] = y;
+                if (!group) {
+                    if (lane == 0) a.logits[row] = y;
+                } else if (lane < a.tp.world) {
+                    a.tp.logits[lane][row] = y;  // every rank's logits buffer (peer stores)
+                }
                 bad |= !isfinite(y);
                 top2_insert(t, y, row);
             }
@@ -486,6 +545,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
         ring_release(ring, g);
     }
     trace_mark(a.trace, 3);
+    if (group) __threadfence_system();  // the logits reach every rank before this rank's top-2 flag
     // Warp results (identical in every lane) -> CTA result -> last CTA merges.
     if (lane == 0) {
         sv[2 * warp] = t.a; sv[2 * warp + 1] = t.b;
@@ -503,7 +563,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
         if (lane == 0) {
             a.pv[2 * blockIdx.x] = u.a; a.pv[2 * blockIdx.x + 1] = u.b;
             a.pi[2 * blockIdx.x] = u.ai; a.pi[2 * blockIdx.x + 1] = u.bi;
-            __threadfence();
+            if (group) __threadfence_system();
+            else __threadfence();
             last = atomicAdd(&a.sync[0], 1u) == gridDim.x - 1;
         }
     }
@@ -526,10 +587,30 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
         }
         top2_merge_warp(z);
         if (lane == 0) {
-            const unsigned flag = atomicExch(&a.sync[1], 0u);
+            unsigned flag = atomicExch(&a.sync[1], 0u);
+            DecodeState *st = a.st;
+            if (group) {
+                // Publish this rank's top-2 to every rank, then merge the
+                // world's (the order of insertion does not change the result).
+                __threadfence_system();
+                const unsigned token = __ldcg(a.tp.epoch) + 1u;
+                const TpTop mine = {z.a, z.b, z.ai, z.bi, flag, {0u, 0u, 0u}};
+                for (int p = 0; p < a.tp.world; p++) a.tp.top[p][a.tp.rank] = mine;
+                __threadfence_system();
+                for (int p = 0; p < a.tp.world; p++) st_release_sys(a.tp.top_flag[p] + a.tp.rank, token);
+                z = top2_empty();
+                flag = 0u;
+                for (int q = 0; q < a.tp.world; q++) {
+                    if (!wait_flag(a.tp.top_flag[a.tp.rank] + q, token, &st->fault)) break;
+                    const volatile TpTop *o = a.tp.top[a.tp.rank] + q;
+                    top2_insert(z, o->a, o->ai);
+                    top2_insert(z, o->b, o->bi);
+                    flag |= o->bad;
+                }
+                *a.tp.epoch = token;
+            }
             TcmTop2 top;
             top.first = z.ai; top.second = z.bi; top.first_value = z.a; top.second_value = z.b;
-            DecodeState *st = a.st;
             st->top = top;
             st->invalid |= (int)flag;
             a.log[st->step % kLogCap] = top;
@@ -660,6 +741,12 @@ struct QwenB200Runner {
     float *pers_part;           // its attention partials
     bool persistent;            // whole tokens run as one persistent launch (when eligible)
     unsigned lookahead;         // its per-CTA L2 prefetch distance (bytes)
+    // Tensor-parallel group (qwen_b200_tp_open / _connect): world 1 when off.
+    TpLink tp;
+    bool tp_on;                 // connected: launches split the MLP and readout
+    unsigned char *tp_area;     // this rank's exchange area (gpu_alloc, exported)
+    void *tp_peer_area[kTpMax], *tp_peer_logits[kTpMax];  // opened peer mappings
+    int tp_rank, tp_world;
 };
 
 int tcm::decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
@@ -686,7 +773,10 @@ template <typename WT> void setup_kernels_typed() {
     set_smem(qkv_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
     set_smem(oproj_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
     set_smem(gateup_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
-    set_smem(down_kernel<WT>, ring_smem_bytes(kDownStages, kDownStage<WT>));
+    set_smem(down_kernel<WT, 1>, ring_smem_bytes(kDownStages, DownGeo<WT, 1>::kStageBytes));
+    set_smem(down_kernel<WT, 2>, ring_smem_bytes(kDownStages, DownGeo<WT, 2>::kStageBytes));
+    set_smem(down_kernel<WT, 4>, ring_smem_bytes(kDownStages, DownGeo<WT, 4>::kStageBytes));
+    set_smem(down_kernel<WT, 8>, ring_smem_bytes(kDownStages, DownGeo<WT, 8>::kStageBytes));
     set_smem(readout_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
 }
 void setup_kernels() {
@@ -791,16 +881,37 @@ template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl,
                    s.qheads / s.kvheads};
     launch(oproj_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
 }
+// The link the launches of a runner carry (world 1 when no group is connected).
+TpLink tp_link(const QwenB200Runner *r) {
+    if (r->tp_on) return r->tp;
+    TpLink t = {};
+    t.world = 1;
+    t.inter = kInter;
+    t.vocab_end = r->d->s.vocab;
+    return t;
+}
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Layer &L = r->d->layers[layer];
-    GateUpArgs g = {L.gate, L.up, L.post_norm, r->b.x, r->b.gate, r->st, trace_slot(r), sched_slot(r, layer, 3),
-                    r->d->s.epsilon};
+    const TpLink t = tp_link(r);
+    const size_t first = (size_t)t.rank * t.inter * kHidden;  // this rank's first unit
+    GateUpArgs g = {(const WT *)L.gate + first, (const WT *)L.up + first, L.post_norm, r->b.x, r->b.gate, r->st,
+                    trace_slot(r), sched_slot(r, layer, 3), r->d->s.epsilon, t.inter};
     launch(gateup_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
 }
+template <typename WT, int SH> void launch_down_sh(QwenB200Runner *r, int layer, bool pdl) {
+    const TpLink t = tp_link(r);
+    DownArgs dn = {(const WT *)r->d->layers[layer].down + (size_t)t.rank * t.inter, r->b.gate, r->b.x, r->st,
+                   trace_slot(r), t, layer};
+    launch(down_kernel<WT, SH>, dim3(r->grid), dim3(kStreamThreads),
+           ring_smem_bytes(kDownStages, DownGeo<WT, SH>::kStageBytes), stream(), pdl, dn);
+}
 template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) {
-    DownArgs dn = {r->d->layers[layer].down, r->b.gate, r->b.x, r->st, trace_slot(r)};
-    launch(down_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kDownStages, kDownStage<WT>), stream(),
-           pdl, dn);
+    switch (r->tp_on ? r->tp.world : 1) {
+        case 2: launch_down_sh<WT, 2>(r, layer, pdl); break;
+        case 4: launch_down_sh<WT, 4>(r, layer, pdl); break;
+        case 8: launch_down_sh<WT, 8>(r, layer, pdl); break;
+        default: launch_down_sh<WT, 1>(r, layer, pdl); break;
+    }
 }
 template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl, bool fold = false) {
     launch_oproj<WT>(r, layer, pdl, fold);
@@ -810,7 +921,7 @@ template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl, b
 template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
     const QwenB200Decoder *d = r->d;
     ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, trace_slot(r),
-                     r->log, sched_slot(r, d->s.layers, 0), d->s.vocab, d->s.epsilon};
+                     r->log, sched_slot(r, d->s.layers, 0), d->s.vocab, d->s.epsilon, tp_link(r)};
     launch(readout_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
            a);
 }
@@ -848,7 +959,7 @@ bool all_served(const QwenB200Runner *r) { return r->ring_on || all_dense(r); }
 int ensure_graph(QwenB200Runner *r);
 bool persistent_ok(const QwenB200Runner *r) {
     const QwenB200Shape &s = r->d->s;
-    return r->pers_layers && !r->ring_on && all_dense(r) && s.kvheads * kPersistAttnCtasPerHead <= r->grid &&
+    return r->pers_layers && !r->ring_on && !r->tp_on && all_dense(r) && s.kvheads * kPersistAttnCtasPerHead <= r->grid &&
            12 * s.layers + 2 <= kPersistMarks && (size_t)r->grid * kPersistMarks <= (size_t)kTraceLaunches * kTraceCtas * 4 &&
            persistent_blocks_per_sm(r->d->dtype) >= 1;
 }
@@ -1035,6 +1146,7 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
 void qwen_b200_runner_free(QwenB200Runner *r) {
     if (!r) return;
     TCM_CUDA(cudaStreamSynchronize(stream()));
+    qwen_b200_tp_close(r);
     drop_graphs(r);
     gpu_free(r->trace);
     gpu_free(r->st);
@@ -1220,7 +1332,8 @@ int qwen_b200_trace_read(QwenB200Runner *r, unsigned long long *host, size_t cou
 
 float qwen_b200_time_stage(QwenB200Runner *r, int stage, int layer, int position, int reps) {
     if (!r || stage < 0 || stage > 5 || layer < 0 || layer >= r->d->s.layers || reps < 1 ||
-        !valid_token(r, 0, position) || (stage == 1 && !has_dense(r, layer) && !r->ring_on))
+        !valid_token(r, 0, position) || (stage == 1 && !has_dense(r, layer) && !r->ring_on) ||
+        (r->tp_on && stage >= 4))  // these stages exchange with the group: only whole tokens
         return -1.f;
     const bool bf16 = r->d->dtype == 2;
     auto once = [&](bool pdl) {
@@ -1271,6 +1384,148 @@ void qwen_b200_ring_rows(void *arena, int rows, int layers, void *save, int writ
     ring_cut_kernel<<<layers, 256, 0, stream()>>>(a);
     TCM_CUDA(cudaGetLastError());
 }
+
+// ---------------------------------------------------------------- tensor-parallel group
+namespace {
+struct TpHandle {
+    char magic[8];
+    int rank, world, grid, layers, vocab, dtype;
+    cudaIpcMemHandle_t area, logits;
+};
+static_assert(sizeof(TpHandle) <= QWEN_B200_TP_HANDLE_BYTES, "the handle must fit its published size");
+constexpr char kTpMagic[8] = "TCMTP01";
+
+typedef int (*AddressRangeFn)(unsigned long long *, size_t *, unsigned long long);
+// The base and size of the allocation holding p (driver cuMemGetAddressRange).
+bool allocation_of(const void *p, unsigned long long *base, size_t *size) {
+    static AddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddressRangeFn>(f);
+    });
+    return fn && fn(base, size, (unsigned long long)(uintptr_t)p) == 0;
+}
+void tp_unmap(QwenB200Runner *r) {
+    for (int p = 0; p < kTpMax; p++) {
+        if (r->tp_peer_area[p]) TCM_CUDA(cudaIpcCloseMemHandle(r->tp_peer_area[p]));
+        if (r->tp_peer_logits[p]) TCM_CUDA(cudaIpcCloseMemHandle(r->tp_peer_logits[p]));
+        r->tp_peer_area[p] = r->tp_peer_logits[p] = nullptr;
+    }
+}
+}  // namespace
+
+int qwen_b200_tp_open(QwenB200Runner *r, int rank, int world, void *handle) {
+    if (!r || !handle || (world != 2 && world != 4 && world != 8) || rank < 0 || rank >= world || r->ring_on ||
+        !all_dense(r) || r->tp_area || r->d->s.intermediate != kInter || r->d->s.vocab < world)
+        return -1;
+    // Peers write the logits through an IPC mapping of their allocation, so the
+    // buffer must be a whole allocation of its own.
+    unsigned long long base = 0;
+    size_t size = 0;
+    if (!allocation_of(r->b.logits, &base, &size) || base != (unsigned long long)(uintptr_t)r->b.logits ||
+        size < (size_t)r->d->s.vocab * sizeof(float)) {
+        fprintf(stderr, "qwen_b200_tp_open: the logits buffer must be the start of its own device allocation\n");
+        return -1;
+    }
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    const TpLayout lay = tp_layout(r->d->s.layers, world, r->grid);
+    r->tp_area = (unsigned char *)gpu_alloc(lay.bytes);
+    gpu_zero(r->tp_area, lay.bytes);
+    TCM_CUDA(cudaStreamSynchronize(stream()));  // zero before any peer can learn the handle
+    TpHandle h = {};
+    memcpy(h.magic, kTpMagic, sizeof(kTpMagic));
+    h.rank = rank;
+    h.world = world;
+    h.grid = r->grid;
+    h.layers = r->d->s.layers;
+    h.vocab = r->d->s.vocab;
+    h.dtype = r->d->dtype;
+    if (cudaIpcGetMemHandle(&h.area, r->tp_area) != cudaSuccess ||
+        cudaIpcGetMemHandle(&h.logits, r->b.logits) != cudaSuccess) {
+        cudaGetLastError();
+        fprintf(stderr, "qwen_b200_tp_open: device memory cannot be exported to peer processes\n");
+        gpu_free(r->tp_area);
+        r->tp_area = nullptr;
+        return -1;
+    }
+    memset(handle, 0, QWEN_B200_TP_HANDLE_BYTES);
+    memcpy(handle, &h, sizeof(h));
+    r->tp_rank = rank;
+    r->tp_world = world;
+    return 0;
+}
+
+int qwen_b200_tp_connect(QwenB200Runner *r, const void *handles) {
+    if (!r || !handles || !r->tp_area || r->tp_on) return -1;
+    const int world = r->tp_world, rank = r->tp_rank;
+    TpHandle hs[kTpMax];
+    for (int p = 0; p < world; p++) {
+        memcpy(&hs[p], (const unsigned char *)handles + (size_t)p * QWEN_B200_TP_HANDLE_BYTES, sizeof(TpHandle));
+        const TpHandle &h = hs[p];
+        if (memcmp(h.magic, kTpMagic, sizeof(kTpMagic)) || h.rank != p || h.world != world || h.grid != r->grid ||
+            h.layers != r->d->s.layers || h.vocab != r->d->s.vocab || h.dtype != r->d->dtype) {
+            fprintf(stderr, "qwen_b200_tp_connect: handle %d does not belong to this group\n", p);
+            return -1;
+        }
+    }
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    const TpLayout lay = tp_layout(r->d->s.layers, world, r->grid);
+    TpLink t = {};
+    for (int p = 0; p < world; p++) {
+        unsigned char *area = r->tp_area;
+        float *logits = r->b.logits;
+        if (p != rank) {
+            void *a = nullptr, *l = nullptr;
+            if (cudaIpcOpenMemHandle(&a, hs[p].area, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+                (r->tp_peer_area[p] = a, cudaIpcOpenMemHandle(&l, hs[p].logits, cudaIpcMemLazyEnablePeerAccess)) !=
+                    cudaSuccess) {
+                cudaGetLastError();
+                fprintf(stderr, "qwen_b200_tp_connect: cannot map rank %d's memory\n", p);
+                tp_unmap(r);
+                return -1;
+            }
+            r->tp_peer_logits[p] = l;
+            area = static_cast<unsigned char *>(a);
+            logits = static_cast<float *>(l);
+        }
+        t.part[p] = reinterpret_cast<float *>(area + lay.part);
+        t.flag[p] = reinterpret_cast<unsigned *>(area + lay.flag);
+        t.logits[p] = logits;
+        t.top[p] = reinterpret_cast<TpTop *>(area + lay.top);
+        t.top_flag[p] = reinterpret_cast<unsigned *>(area + lay.top_flag);
+    }
+    t.epoch = reinterpret_cast<unsigned *>(r->tp_area + lay.epoch);
+    t.rank = rank;
+    t.world = world;
+    t.inter = kInter / world;
+    t.vocab_begin = share_begin(r->d->s.vocab, rank, world);
+    t.vocab_end = share_begin(r->d->s.vocab, rank + 1, world);
+    drop_graphs(r);
+    r->tp = t;
+    r->tp_on = true;
+    return 0;
+}
+
+int qwen_b200_tp_close(QwenB200Runner *r) {
+    if (!r) return -1;
+    if (!r->tp_area) return 0;
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    drop_graphs(r);
+    tp_unmap(r);
+    gpu_free(r->tp_area);
+    r->tp_area = nullptr;
+    r->tp_on = false;
+    r->tp = TpLink{};
+    r->tp_rank = 0;
+    r->tp_world = 0;
+    return 0;
+}
+
+int qwen_b200_tp_world(const QwenB200Runner *r) { return r && r->tp_on ? r->tp.world : 1; }
 
 void qwen_b200_mark(int index) {
     int dev = 0;

@@ -143,6 +143,6 @@ template <typename WT> __device__ __forceinline__ float row_dot(const unsigned c
 }
 
 
-__device__ __forceinline__ int share_begin(int total, int part, int parts) { return (int)((long long)part * total / parts); }
+__host__ __device__ __forceinline__ int share_begin(int total, int part, int parts) { return (int)((long long)part * total / parts); }
 
 }  // namespace tcm

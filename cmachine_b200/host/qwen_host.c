@@ -373,6 +373,8 @@ int qwen_advance_layer(QwenSession *s) {
     const QwenModel *m = s->model;
     if (s->phase != 2 || s->layer >= m->layers) return -1;
     const int i = s->layer;
+    /* A tensor-parallel group runs only its fused split layers. */
+    if (s->runner && observing(s, i) && qwen_b200_tp_world(s->runner) > 1) return -1;
     int error = (s->runner && !observing(s, i)) ? fused_layer(s, i) : primitive_layer(s, i);
     if (error) return error;
     s->layer++;
@@ -636,4 +638,18 @@ int qwen_reset(QwenSession *s) {
     s->token_parent_valid = 0;
     if (s->cache_rewind) s->cache_rewind(s->cache_context, 0, s->session_id, s->epoch);
     return 0;
+}
+
+/* Tensor-parallel decode over several GPUs (include/qwen_b200.h). */
+int qwen_session_tp_open(QwenSession *s, int rank, int world, void *handle) {
+    if (!s || !s->runner || s->cache_mask || s->phase == 2) return -1;
+    return qwen_b200_tp_open(s->runner, rank, world, handle);
+}
+int qwen_session_tp_connect(QwenSession *s, const void *handles) {
+    if (!s || !s->runner || s->phase == 2) return -1;
+    return qwen_b200_tp_connect(s->runner, handles);
+}
+int qwen_session_tp_close(QwenSession *s) {
+    if (!s || !s->runner) return -1;
+    return qwen_b200_tp_close(s->runner);
 }

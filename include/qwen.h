@@ -177,6 +177,19 @@ int qwen_push_batch(QwenSession **sessions, int n, const int *tokens);
  * it stay pushed. */
 int qwen_prefill(QwenSession *, const int *tokens, int n);
 
+/* B200 addition: tensor-parallel decode of one session over `world` GPUs (2, 4
+ * or 8), one process per GPU, each with the whole model and its own copy of the
+ * session (qwen_b200_tp_open/_connect/_close in include/qwen_b200.h, applied
+ * to the session's runner). Open on every rank, gather the handles
+ * (QWEN_B200_TP_HANDLE_BYTES each) in rank order, connect; then every rank
+ * pushes the same tokens. While connected, a layer with an armed observer
+ * (which would run the single-GPU primitive path) is refused. Requires the
+ * fused decoder and every layer's K/V in the session. 0 or -1 (nothing
+ * changed). */
+int qwen_session_tp_open(QwenSession *, int rank, int world, void *handle);
+int qwen_session_tp_connect(QwenSession *, const void *handles);
+int qwen_session_tp_close(QwenSession *);
+
 #ifdef __cplusplus
 }
 #endif

@@ -205,6 +205,41 @@ int qwen_b200_batch_cluster_capacity(int size);
 int qwen_b200_batch_tune(QwenB200Batch *, int key, int value);
 int qwen_b200_batch_clusters(const QwenB200Batch *, int *qkv, int *o, int *down);
 
+/* ---- Tensor-parallel decode of one session over several GPUs ----
+ * One process per GPU, each holding the whole model and its own copy of the
+ * session (same prompt, same tokens). A connected group splits every MLP (each
+ * rank computes 8960/world of the intermediate units: its rows of gate and up,
+ * its columns of down) and the tied-embedding readout (rows
+ * [rank*V/world, (rank+1)*V/world)), the work the reference does at
+ * src/qwen.c:320,329-330,341 and 383-387. After each layer's down projection
+ * the ranks exchange partial residual sums through each other's memory (peer
+ * stores over NVLink, per-CTA flags) and add them in rank order, so every rank
+ * keeps a bit-identical residual stream and K/V cache; after the readout they
+ * exchange top-2s (ties to the lower id) and every rank's logits buffer
+ * receives all ranks' logits. Numerically this changes only the order of the
+ * down projection's sum. world is 2, 4 or 8; every layer must keep its K/V in
+ * the session (no ring). Steps:
+ *   1. qwen_b200_tp_open on every rank: allocates the rank's exchange area and
+ *      writes QWEN_B200_TP_HANDLE_BYTES of handle (CUDA IPC handles of the area
+ *      and of the session's logits buffer, which must be a whole allocation);
+ *   2. the caller gathers the world's handles in rank order (any transport,
+ *      e.g. torch.distributed all_gather) and calls qwen_b200_tp_connect;
+ *   3. all ranks then run the same whole tokens (qwen_push, qwen_advance,
+ *      qwen_generate, qwen_b200_enqueue) in lockstep, each starting a token
+ *      within the 2 s wait limit of the others. The stage calls of a layer's
+ *      MLP and the readout exchange too and must also be made by every rank.
+ * Returns 0 or -1 (invalid arguments, a handle of another group, memory that
+ * cannot be exported or mapped; nothing changed). A wait that runs out marks
+ * the token's fault (-4 from the token calls); the group must then be closed
+ * and rebuilt. qwen_b200_tp_close (also done by qwen_b200_runner_free) unmaps
+ * the peers and frees the area: close on every rank after a final barrier. */
+#define QWEN_B200_TP_HANDLE_BYTES 256
+int qwen_b200_tp_open(QwenB200Runner *, int rank, int world, void *handle);
+int qwen_b200_tp_connect(QwenB200Runner *, const void *handles);
+int qwen_b200_tp_close(QwenB200Runner *);
+/* The connected group's size, or 1. */
+int qwen_b200_tp_world(const QwenB200Runner *);
+
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Whole-token execution: 1 = one persistent cooperative launch per token (one

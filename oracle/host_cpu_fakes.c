@@ -111,3 +111,7 @@ int qwen_b200_batch_step(QwenB200Batch *b, int n, const QwenB200BatchSession *s,
     (void)b; (void)n; (void)s; (void)t; (void)p; (void)o;
     return -1;
 }
+int qwen_b200_tp_open(QwenB200Runner *r, int rank, int world, void *h) { (void)r; (void)rank; (void)world; (void)h; return -1; }
+int qwen_b200_tp_connect(QwenB200Runner *r, const void *h) { (void)r; (void)h; return -1; }
+int qwen_b200_tp_close(QwenB200Runner *r) { (void)r; return -1; }
+int qwen_b200_tp_world(const QwenB200Runner *r) { (void)r; return 1; }
