@@ -186,6 +186,8 @@ def _declare(L, strict: bool = True):
         "qwen_b200_session_set_cursor": (c_int, [P, c_int, c_int]),
         "qwen_session_tp_open": (c_int, [P, c_int, c_int, P]), "qwen_session_tp_connect": (c_int, [P, P]),
         "qwen_session_tp_close": (c_int, [P]), "qwen_b200_tp_world": (c_int, [P]),
+        "qwen_b200_wait_limit": (c_int, [ctypes.c_ulonglong]),
+        "qwen_b200_pipeline_check": (c_int, [P, c_int, P, P, c_int]),
         "qwen_b200_unregister_matrix": (None, [P]),
         # host/session_view.c
         "qwen_b200_model_size": (c_size_t, []), "qwen_b200_session_size": (c_size_t, []),

@@ -1093,6 +1093,8 @@ struct LayerMaps {
     CUtensorMap q, k, v, o, gate, up, down;
 };
 
+void set_wait_limit_batch(unsigned long long ns) { set_module_wait_limit(ns); }
+
 }  // namespace tcm
 
 using namespace tcm;

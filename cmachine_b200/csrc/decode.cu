@@ -673,6 +673,47 @@ __global__ void __launch_bounds__(256) ring_cut_kernel(RingCutArgs a) {
     }
 }
 
+// ---------------------------------------------------------------- pipeline self-check
+// One CTA streams `rows` FP32 rows of 1536 through the same shared-memory ring
+// the decode GEMVs use and forms y = W x. With `starve` the producer is told to
+// issue nothing, so every consumer warp's first wait runs out at the wait limit,
+// records kErrFullWait and returns: no copy is in flight, nothing is left held.
+struct SelfCheckArgs {
+    const float *w, *x;
+    float *y;
+    unsigned *fault;
+    int rows, starve;
+};
+__global__ void __launch_bounds__(kStreamThreads, 1) ring_selfcheck_kernel(SelfCheckArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int R = Geo<float>::R;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const Ring ring = ring_setup(smem, kStages, kStage<float>);
+    if (warp == kConsumerWarps) {
+        if (lane == 0)
+            ring_produce(ring, a.starve ? 0 : a.rows, R, kRow<float>,
+                         [&](int i) { return (const void *)(a.w + (size_t)i * kHidden); }, a.fault);
+        return;
+    }
+    float xr[kLaneX];
+    load_lane_vec<float>(xr, a.x, lane);
+    const int groups = (a.rows + R - 1) / R;
+    for (int g = 0; g < groups; g++) {
+        if (!ring_acquire(ring, g, a.fault)) break;
+        const int n = min(R, a.rows - g * R);
+        const unsigned char *stage = ring.stage(g % kStages);
+#pragma unroll
+        for (int m = 0; m < R / kConsumerWarps; m++) {
+            const int j = warp + kConsumerWarps * m;
+            if (j < n) {
+                const float y = row_dot<float>(stage + (size_t)j * kRow<float>, xr, lane);
+                if (lane == 0) a.y[g * R + j] = y;
+            }
+        }
+        ring_release(ring, g);
+    }
+}
+
 // Token state from kernel arguments: nothing in host memory is read after the
 // launch call returns, so chained enqueues never race a host buffer.
 __global__ void set_state_kernel(DecodeState *st, int token, int position) {
@@ -691,6 +732,8 @@ template <typename T> inline void set_smem(T *kernel, size_t bytes) {
 }
 
 }  // namespace
+
+void set_wait_limit_decode(unsigned long long ns) { set_module_wait_limit(ns); }
 
 __global__ void seeded_fill_kernel(void *dst, int dtype, uint64_t base, size_t n, TcmFill f) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
@@ -778,6 +821,7 @@ template <typename WT> void setup_kernels_typed() {
     set_smem(down_kernel<WT, 4>, ring_smem_bytes(kDownStages, DownGeo<WT, 4>::kStageBytes));
     set_smem(down_kernel<WT, 8>, ring_smem_bytes(kDownStages, DownGeo<WT, 8>::kStageBytes));
     set_smem(readout_kernel<WT>, ring_smem_bytes(kStages, kStage<WT>));
+    set_smem(ring_selfcheck_kernel, ring_smem_bytes(kStages, kStage<float>));
 }
 void setup_kernels() {
     static PerDeviceOnce once;
@@ -1526,6 +1570,30 @@ int qwen_b200_tp_close(QwenB200Runner *r) {
 }
 
 int qwen_b200_tp_world(const QwenB200Runner *r) { return r && r->tp_on ? r->tp.world : 1; }
+
+int qwen_b200_wait_limit(unsigned long long ns) {
+    if (ns == 0) ns = kWaitLimitNs;
+    if (ns < kWaitFloorNs || ns > 60000000000ull) return -1;
+    TCM_CUDA(cudaStreamSynchronize(stream()));
+    set_module_wait_limit(ns);  // this file's kernels
+    set_wait_limit_persistent(ns);
+    set_wait_limit_batch(ns);
+    return 0;
+}
+
+int qwen_b200_pipeline_check(const float *w, int rows, const float *x, float *y, int starve) {
+    if (!w || !x || !y || rows < 1 || rows > 4096 || ((uintptr_t)w & 15) || ((uintptr_t)x & 15)) return -1;
+    setup_kernels();
+    unsigned *fault = (unsigned *)gpu_alloc(sizeof(unsigned));
+    gpu_zero(fault, sizeof(unsigned));
+    SelfCheckArgs a = {w, x, y, fault, rows, starve ? 1 : 0};
+    launch(ring_selfcheck_kernel, dim3(1), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<float>), stream(), false,
+           a);
+    unsigned bits = 0;
+    gpu_read(&bits, fault, sizeof(bits));
+    gpu_free(fault);
+    return (int)bits;
+}
 
 void qwen_b200_mark(int index) {
     int dev = 0;

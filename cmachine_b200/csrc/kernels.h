@@ -36,4 +36,10 @@ int weight_dtype(const void *p);
 int decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
                  const float **final_norm, const float **rope_den, int *dtype);
 
+// The bound of every bounded wait in each kernel module, for the current
+// device (qwen_b200_wait_limit sets them all).
+void set_wait_limit_decode(unsigned long long ns);
+void set_wait_limit_persistent(unsigned long long ns);
+void set_wait_limit_batch(unsigned long long ns);
+
 }  // namespace tcm

@@ -39,6 +39,7 @@
 #include "stream.cuh"
 #include "lanes.cuh"
 #include "persistent.cuh"
+#include "kernels.h"
 #include <mutex>
 
 namespace tcm {
@@ -116,7 +117,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, unsig
     for (;;) {
         if (mbar_try(bar, parity)) return true;
         if (aborted(abort_s)) return false;
-        if (global_ns() - start > kWaitLimitNs) {
+        if (wait_expired(global_ns() - start)) {
             atomicOr(err, code);
             *abort_s = 1;
             return false;
@@ -338,7 +339,7 @@ __device__ __forceinline__ void grid_barrier(DecodeState *st, unsigned target, v
                     *abort_s = 1;
                     break;
                 }
-                if (global_ns() - start > kWaitLimitNs) {
+                if (wait_expired(global_ns() - start)) {
                     atomicOr(&st->fault, kErrGrid);
                     *abort_s = 1;
                     break;
@@ -823,6 +824,8 @@ template <typename WT> int setup_typed() {
 }
 
 }  // namespace
+
+void set_wait_limit_persistent(unsigned long long ns) { set_module_wait_limit(ns); }
 
 int persistent_blocks_per_sm(int dtype) {
     static PerDeviceOnce once;

@@ -8,10 +8,11 @@
 // before griddepcontrol.wait: while the previous kernel drains, this kernel's
 // first stages are already in flight.
 //
-// Every wait is bounded in time: after kWaitLimitNs of polling (global timer)
-// the waiter records an error bit in the caller's error word and returns
-// false; the caller then stops, and the producer waits (again bounded) for the
-// copies it issued before it exits.
+// Every wait is bounded in time: after the wait limit of polling (global timer;
+// kWaitLimitNs unless qwen_b200_wait_limit set another) the waiter records an
+// error bit in the caller's error word and returns false; the caller then
+// stops, and the producer waits (again bounded) for the copies it issued
+// before it exits.
 #pragma once
 #include "common.cuh"
 
@@ -19,7 +20,20 @@ namespace tcm {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kStreamThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s, the default bound of a wait
+constexpr unsigned long long kWaitFloorNs = 1000000ull;     // 1 ms: no wait gives up sooner
+
+// The bound of this module's waits. Every .cu file that includes this header
+// has its own copy (no device linking); set_module_wait_limit sets it for the
+// current device. It is read only once a wait has lasted kWaitFloorNs, so the
+// fast path never loads it.
+static __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+__device__ __forceinline__ bool wait_expired(unsigned long long elapsed) {
+    return elapsed > kWaitFloorNs && elapsed > g_wait_limit_ns;
+}
+static inline void set_module_wait_limit(unsigned long long ns) {
+    TCM_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)));
+}
 
 enum : unsigned { kErrFullWait = 1u, kErrEmptyWait = 2u, kErrDrain = 4u };
 
@@ -57,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     const unsigned long long start = global_ns();
     for (;;) {
         if (mbar_try(bar, parity)) return true;
-        if (global_ns() - start > kWaitLimitNs) {
+        if (wait_expired(global_ns() - start)) {
             atomicOr(err, code);
             return false;
         }

@@ -21,7 +21,7 @@
 //
 // Flags carry the token's number (the exchange area's epoch + 1), so they never
 // need clearing; a rank cannot reach the same flag of the next token before
-// every rank has passed this one. Every wait is bounded (kWaitLimitNs) and
+// every rank has passed this one. Every wait is bounded (the wait limit) and
 // records a fault bit; after a fault the group must be rebuilt. No TMA and no
 // multicast: peer memory is written with plain stores and read locally.
 #pragma once
@@ -72,7 +72,7 @@ __device__ __forceinline__ bool wait_flag(const unsigned *p, unsigned want, unsi
     const unsigned long long start = global_ns();
     for (;;) {
         if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
-        if (global_ns() - start > kWaitLimitNs) {
+        if (wait_expired(global_ns() - start)) {
             atomicOr(err, kErrPeerWait);
             return false;
         }

@@ -240,6 +240,19 @@ int qwen_b200_tp_close(QwenB200Runner *);
 /* The connected group's size, or 1. */
 int qwen_b200_tp_world(const QwenB200Runner *);
 
+/* ---- Bounded waits ----
+ * Every wait inside the kernels (a pipeline stage, a grid barrier, a peer's
+ * flag) gives up after a time limit, records a fault bit and lets its kernel
+ * return; the token calls then report -4. qwen_b200_wait_limit sets that limit
+ * for the current device (ns; 0 restores the default 2 s; 1 ms .. 60 s,
+ * else -1). qwen_b200_pipeline_check runs the decode GEMVs' shared-memory ring
+ * on one CTA: y[rows] = W[rows][1536] x (FP32 device pointers, rows <= 4096)
+ * and returns the fault bits (0 when every wait completed; with starve != 0
+ * the producer issues nothing, so the consumers' waits run out: bit 1), or -1
+ * for invalid arguments. */
+int qwen_b200_wait_limit(unsigned long long ns);
+int qwen_b200_pipeline_check(const float *w, int rows, const float *x, float *y, int starve);
+
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Whole-token execution: 1 = one persistent cooperative launch per token (one
