@@ -160,3 +160,15 @@ int orc_set_cursor(void *p, int position) {
  * reference host over the B200 primitives. */
 int orc_stack_push(void *p, uint64_t *id) { return qwen_stack_push((QwenSession *)p, id); }
 int orc_stack_rollback(void *p, uint64_t id) { return qwen_stack_rollback((QwenSession *)p, id); }
+
+/* The model as the reference's qwen_model_free expects it: the tensors listed
+ * in allocations (the serve build takes ownership of the descriptor). */
+QwenModel *orc_model_take(void *p) {
+    RefModel *r = p;
+    QwenModel *m = &r->model;
+    m->allocations = calloc(r->count ? r->count : 1, sizeof(float *));
+    if (!m->allocations) abort();
+    for (unsigned i = 0; i < r->count; i++) m->allocations[i] = r->slots[i];
+    m->allocation_count = r->count;
+    return m;
+}

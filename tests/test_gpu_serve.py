@@ -126,3 +126,52 @@ def test_bundle_serves_as_the_seeded_model(tmp_path):
             assert a["cache_sha256"] == b["cache_sha256"] and a["logits_sha256"] == b["logits_sha256"]
         else:
             assert a == b
+
+
+REF_SERVE = ROOT / "oracle" / "_ref" / "ref-serve-cpu"
+# Reply fields that hold floating-point state or memory accounting: the B200
+# path computes within FP32 tolerance of the reference's CPU path, not to its bits.
+NUMERIC = {"cache_sha256", "logits_sha256", "gpu_weight_bytes", "gpu_session_bytes", "gpu_state_bytes",
+           "tracked_gpu_bytes", "weight_storage"}
+
+
+def ref_run(model, commands, *args):
+    proc = subprocess.run([str(REF_SERVE), "serve", model, *args], input="\n".join(commands) + "\n", text=True,
+                          capture_output=True, timeout=900)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    return [json.loads(line) for line in proc.stdout.splitlines()]
+
+
+def replay_matches(model, commands, *args):
+    ours, ref = run(model, commands, *args), ref_run(model, commands, *args)
+    assert len(ours) == len(ref)
+    for i, (a, b) in enumerate(zip(ours, ref)):
+        assert set(a) == set(b), (i, a, b)
+        for key in a:
+            if key not in NUMERIC:
+                assert a[key] == b[key], (i, key, a[key], b[key])
+    return ours, ref
+
+
+@pytest.mark.skipif(not REF_SERVE.exists(), reason="reference serve build absent")
+def test_dense_protocol_replay_against_reference_serve():
+    """The same scripted session through the B200 tcm-cuda and the reference's
+    own serve loop (src/qwen_serve.c over its CPU FP32 path): every reply field
+    but the float hashes and byte counts, generated ids included. 2-layer FP32
+    seeded model (full Qwen2.5-1.5B widths)."""
+    script = ["A " + prompt(12, 5), "G 6", "S", "P", "A " + prompt(3, 6), "S", "B 1", "S", "C", "A 7", "R", "S",
+              "P", "P", "A 4", "K 3", "B 2", "Z", "S", "A 11 12", "G 4", "S", "Q"]
+    ours, _ = replay_matches("seeded:qwen2.5-1.5b@2:21:0", script, "--context", "64")
+    assert sum(len(r.get("ids", [])) for r in ours) == 10
+
+
+@pytest.mark.skipif(not REF_SERVE.exists(), reason="reference serve build absent")
+def test_bounded_protocol_replay_against_reference_serve():
+    """A bounded byte-codec session (retention 2/4/3, evicting and sampling the
+    reservoir) through the B200 tcm-cuda and the reference's bounded serve
+    (src/qwen_bounded_serve.c + src/bounded_cache.h over its CPU path): cursor,
+    evictions, RNG state, resident rows, frames and generated ids must agree.
+    28-layer FP32 seeded model, as the reference ring requires."""
+    script = ["A " + prompt(9, 8), "G 3", "S", "P", "A 5 6", "S", "B 1", "S", "Q"]
+    replay_matches("seeded:qwen2.5-1.5b:22:0", script, "--cache-policy", "bounded", "--context", "64", "--anchors",
+                   "2", "--recent", "4", "--reservoir", "3")

@@ -56,32 +56,35 @@ def _rank(rank, world, port, profile, out):
         assert status == 0, "tp_open"
         assert s.tp_connect(cm.tp_gather(dist, handle)) == 0, "tp_connect"
         assert s.tp_world == world
-        oracle = CpuDecoder(ORACLE, shape, seed, cm.TEST_LAW, profile == 2, 64) if rank == 0 else None
-        single = cm.Session(model, 64) if rank == 0 else None  # a second session, decoded on this GPU alone
         dist.barrier()
+        # The group's tokens first, back to back on both ranks (the checks on
+        # the CPU come after, so no rank lags the other by host work).
         tokens = [int(t) for t in np.random.default_rng(seed).integers(0, shape.vocab, 6)]
-        worst_oracle = worst_single = 0.0
-        digests = []
-        steps = len(tokens) + 10
-        for i in range(steps):
+        fed, seen, digests = [], [], []
+        for i in range(len(tokens) + 10):
             token = tokens[i] if i < len(tokens) else s.pending
             assert s.push(token) == 0, f"push {i}"
+            fed.append(token)
             logits = s.logits()
+            seen.append(logits)
             digests.append(hashlib.sha256(logits.tobytes() + repr(s.top).encode()).hexdigest())
-            if rank == 0:
+        kv = hashlib.sha256(b"".join(s.kv(l, k).tobytes() for l in range(shape.layers) for k in (0, 1))).hexdigest()
+        dist.barrier()
+        assert s.tp_close() == 0
+        dist.barrier()
+        worst_oracle = worst_single = 0.0
+        if rank == 0:
+            oracle = CpuDecoder(ORACLE, shape, seed, cm.TEST_LAW, profile == 2, 64)
+            single = cm.Session(model, 64)  # the same tokens on this GPU alone
+            for token, logits in zip(fed, seen):
                 _, want = oracle.push(token)
                 worst_oracle = max(worst_oracle, float(np.max(np.abs(logits - want))))
                 assert single.push(token) == 0
                 worst_single = max(worst_single, float(np.max(np.abs(logits - single.logits()))))
-        kv = hashlib.sha256(b"".join(s.kv(l, k).tobytes() for l in range(shape.layers) for k in (0, 1))).hexdigest()
-        result.update(digests=digests, kv=kv, worst_oracle=worst_oracle, worst_single=worst_single,
-                      position=s.position)
-        dist.barrier()
-        assert s.tp_close() == 0
-        dist.barrier()
-        if rank == 0:
             oracle.close()
             single.free()
+        result.update(digests=digests, kv=kv, worst_oracle=worst_oracle, worst_single=worst_single,
+                      position=s.position)
         s.free()
         model.free()
     except Exception as e:  # reported to the parent
