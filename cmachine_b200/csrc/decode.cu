@@ -411,6 +411,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
     }
     trace_mark(a.trace, 2);
     constexpr bool group = SH > 1;  // a rank reads part of each row only inside a group
+    const unsigned token = group ? __ldcg(a.tp.epoch) + 1u : 0u;
     const int groups = (items + RD - 1) / RD;
     for (int g = 0; g < groups; g++) {
         const int n = min(RD, items - g * RD);
@@ -441,32 +442,25 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
             for (int p = 1; p < PIECES; p++) sum = __fadd_rn(sum, part_s[g & 1][s][p]);
             if (group) {
                 const size_t at = ((size_t)a.layer * a.tp.world + a.tp.rank) * kHidden + row;
-                for (int p = 0; p < a.tp.world; p++) a.tp.part[p][at] = sum;  // peer stores over NVLink
+                for (int p = 0; p < a.tp.world; p++) ll_store(a.tp.part[p] + at, __float_as_uint(sum), token);
             } else {
                 a.x[row] = __fadd_rn(a.x[row], sum);
             }
         }
     }
     if (group && !fail_s) {
-        // This CTA's partial rows are in every rank's area: raise its flag at
-        // each rank, wait for the same CTA of every rank, then add the world
-        // partials of these rows in rank order.
-        __threadfence_system();
-        consumers_sync();
-        const unsigned token = __ldcg(a.tp.epoch) + 1u;
-        const size_t fslot = ((size_t)a.layer * gridDim.x + blockIdx.x) * a.tp.world;
-        if ((int)threadIdx.x < a.tp.world) {
-            st_release_sys(a.tp.flag[threadIdx.x] + fslot + a.tp.rank, token);
-            if (!wait_flag(a.tp.flag[a.tp.rank] + fslot + threadIdx.x, token, &a.st->fault)) fail_s = 1;
-        }
-        consumers_sync();
-        if (!fail_s) {
-            const float *mine = a.tp.part[a.tp.rank] + (size_t)a.layer * a.tp.world * kHidden;
-            for (int row = r0 + (int)threadIdx.x; row < r1; row += kConsumerWarps * 32) {
-                float sum = __ldcv(mine + row);
-                for (int p = 1; p < a.tp.world; p++) sum = __fadd_rn(sum, __ldcv(mine + (size_t)p * kHidden + row));
-                a.x[row] = __fadd_rn(a.x[row], sum);
+        // This CTA's partial rows are on their way to every rank; add the
+        // world's partials of the same rows, in rank order, as they arrive.
+        const unsigned long long *mine = a.tp.part[a.tp.rank] + (size_t)a.layer * a.tp.world * kHidden;
+        for (int row = r0 + (int)threadIdx.x; row < r1; row += kConsumerWarps * 32) {
+            float sum = 0.f;
+            bool ok = true;
+            for (int p = 0; p < a.tp.world && ok; p++) {
+                unsigned bits = 0;
+                ok = ll_wait(mine + (size_t)p * kHidden + row, token, &bits, &a.st->fault);
+                sum = p ? __fadd_rn(sum, __uint_as_float(bits)) : __uint_as_float(bits);
             }
+            if (ok) a.x[row] = __fadd_rn(a.x[row], sum);
         }
     }
     trace_mark(a.trace, 3);
@@ -592,21 +586,27 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
             if (group) {
                 // Publish this rank's top-2 to every rank, then merge the
                 // world's (the order of insertion does not change the result).
+                // The fence orders every CTA's logits stores (each CTA fenced
+                // before counting itself done) before the published words.
                 __threadfence_system();
                 const unsigned token = __ldcg(a.tp.epoch) + 1u;
-                const TpTop mine = {z.a, z.b, z.ai, z.bi, flag, {0u, 0u, 0u}};
-                for (int p = 0; p < a.tp.world; p++) a.tp.top[p][a.tp.rank] = mine;
-                __threadfence_system();
-                for (int p = 0; p < a.tp.world; p++) st_release_sys(a.tp.top_flag[p] + a.tp.rank, token);
+                const unsigned words[5] = {__float_as_uint(z.a), __float_as_uint(z.b), (unsigned)z.ai, (unsigned)z.bi,
+                                           flag};
+                for (int p = 0; p < a.tp.world; p++)
+                    for (int w = 0; w < 5; w++) ll_store(a.tp.top[p] + a.tp.rank * kTpTopWords + w, words[w], token);
                 z = top2_empty();
                 flag = 0u;
                 for (int q = 0; q < a.tp.world; q++) {
-                    if (!wait_flag(a.tp.top_flag[a.tp.rank] + q, token, &st->fault)) break;
-                    const volatile TpTop *o = a.tp.top[a.tp.rank] + q;
-                    top2_insert(z, o->a, o->ai);
-                    top2_insert(z, o->b, o->bi);
-                    flag |= o->bad;
+                    unsigned v[5];
+                    bool ok = true;
+                    for (int w = 0; w < 5 && ok; w++)
+                        ok = ll_wait(a.tp.top[a.tp.rank] + q * kTpTopWords + w, token, &v[w], &st->fault);
+                    if (!ok) break;
+                    top2_insert(z, __uint_as_float(v[0]), (int)v[2]);
+                    top2_insert(z, __uint_as_float(v[1]), (int)v[3]);
+                    flag |= v[4];
                 }
+                __threadfence_system();  // the peers' logits stores are visible past this kernel's end
                 *a.tp.epoch = token;
             }
             TcmTop2 top;
@@ -1476,7 +1476,7 @@ int qwen_b200_tp_open(QwenB200Runner *r, int rank, int world, void *handle) {
         return -1;
     }
     TCM_CUDA(cudaStreamSynchronize(stream()));
-    const TpLayout lay = tp_layout(r->d->s.layers, world, r->grid);
+    const TpLayout lay = tp_layout(r->d->s.layers, world);
     r->tp_area = (unsigned char *)gpu_alloc(lay.bytes);
     gpu_zero(r->tp_area, lay.bytes);
     TCM_CUDA(cudaStreamSynchronize(stream()));  // zero before any peer can learn the handle
@@ -1517,7 +1517,7 @@ int qwen_b200_tp_connect(QwenB200Runner *r, const void *handles) {
         }
     }
     TCM_CUDA(cudaStreamSynchronize(stream()));
-    const TpLayout lay = tp_layout(r->d->s.layers, world, r->grid);
+    const TpLayout lay = tp_layout(r->d->s.layers, world);
     TpLink t = {};
     for (int p = 0; p < world; p++) {
         unsigned char *area = r->tp_area;
@@ -1536,11 +1536,9 @@ int qwen_b200_tp_connect(QwenB200Runner *r, const void *handles) {
             area = static_cast<unsigned char *>(a);
             logits = static_cast<float *>(l);
         }
-        t.part[p] = reinterpret_cast<float *>(area + lay.part);
-        t.flag[p] = reinterpret_cast<unsigned *>(area + lay.flag);
+        t.part[p] = reinterpret_cast<unsigned long long *>(area + lay.part);
         t.logits[p] = logits;
-        t.top[p] = reinterpret_cast<TpTop *>(area + lay.top);
-        t.top_flag[p] = reinterpret_cast<unsigned *>(area + lay.top_flag);
+        t.top[p] = reinterpret_cast<unsigned long long *>(area + lay.top);
     }
     t.epoch = reinterpret_cast<unsigned *>(r->tp_area + lay.epoch);
     t.rank = rank;

@@ -10,6 +10,11 @@ done. Per phase (q/k/v, attention, merge, O, gate/up, down) the report gives the
 mean over layers of the time from the previous barrier's release (its first
 CTA through) to this one's, and how far apart the CTAs passed it.
 
+Under torchrun with 2, 4 or 8 processes the session is split tensor-parallel
+over the GPUs (MLP units and readout rows, peer-memory exchanges in the down
+projection and the readout); every rank traces its own kernels and prints its
+own report.
+
 Token graph: every CTA of every launch stamps the GPU global timer at entry, when its
 dependency on the previous launch was released (griddepcontrol.wait), when its
 input vector was ready and when it finished. Per stage kind the report gives the
@@ -65,8 +70,20 @@ def main():
     ap.add_argument("--time", type=int, default=0, help="then time this many chained greedy tokens (device time)")
     args = ap.parse_args()
     L = cm.lib()
+    import os
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        import torch.distributed as dist
+        L.qwen_b200_set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
     model = cm.Model(cm.qwen_shape(args.layers, 32768), 2026, cm.BENCH_LAW, args.profile)
     s = cm.Session(model, args.prompt + args.tokens + 9 + args.time)
+    if world > 1:
+        status, handle = s.tp_open(rank, world)
+        assert status == 0 and s.tp_connect(cm.tp_gather(dist, handle)) == 0
+        dist.barrier()
+        print(f"rank {rank}: tensor-parallel over {world} GPUs", flush=True)
     for i in range(args.prompt):
         assert s.push((i * 7919 + 11) % model.shape.vocab) == 0
     runner = s.runner
@@ -108,7 +125,7 @@ def main():
         rec["boundary"] = rec["release0"] - prev_done if prev_done is not None else np.nan
         prev_done = rec["done1"]
         rows.append(rec)
-    print(f"launches recorded: {n}; token span {rows[-1]['done1'] / 1000:.1f} us")
+    print(f"rank {rank}: launches recorded: {n}; token span {rows[-1]['done1'] / 1000:.1f} us")
     print(f"{'stage':10s} {'boundary':>9s} {'rel->ready':>10s} {'ready->done':>11s} {'span':>8s} "
           f"{'rel spread':>10s} {'cta ready':>9s} {'cta work':>9s} {'done spread':>11s} {'resident':>8s}"
           f"   (us, mean over layers; resident = a CTA's entry to its release, median)")
@@ -134,6 +151,10 @@ def main():
             L.gpu_sync()
             ms = L.qwen_b200_elapsed_ms(0, 1) / args.time
             print(f"{ms * 1000:.1f} us/token ({1000 / ms:.1f} tokens/s) over {args.time} chained tokens")
+    if world > 1:
+        dist.barrier()
+        s.tp_close()
+        dist.barrier()
     s.free()
     model.free()
 

@@ -59,3 +59,22 @@ def test_reference_host_over_b200_primitives():
     finally:
         ref.close()
         oracle.close()
+
+
+GPU_MECHANICS = REF_GPUHOST.parent / "gpu-mechanics-b200"
+
+
+@pytest.mark.skipif(not GPU_MECHANICS.exists(), reason="reference GPU mechanics build absent")
+def test_reference_gpu_mechanics_on_b200_primitives():
+    """The reference's own GPU test (tests/gpu_mechanics.c, unchanged) linked
+    against this library instead of its cuBLAS object: exact matvec {5, 5, 1},
+    attention and RoPE within 2e-5 of double precision, top-2 ties to the lower
+    id, and checkpoint ownership, all asserted by the reference's code."""
+    import json
+    import subprocess
+    proc = subprocess.run([str(GPU_MECHANICS)], capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    out = json.loads(proc.stdout.strip().splitlines()[-1])
+    print(out)
+    assert out["matvec_exact"] and out["top2_ties"] and out["checkpoint_ownership"]
+    assert out["attention_max_error"] < 2e-5 and out["rope_max_error"] < 2e-5
