@@ -96,7 +96,7 @@ static int seeded_shape(const char *text, QwenB200Shape *s) {
 
 /* A bundle path, or seeded:SHAPE:SEED:PROFILE (weights N(0, 0.02), norms 1,
  * biases 0). `profile` is the bundle's weight profile. */
-static int open_model(QwenModel *m, const char *spec, int profile, char *error, size_t capacity) {
+int qwen_model_open(QwenModel *m, const char *spec, int profile, char *error, size_t capacity) {
     if (!strncmp(spec, "seeded:", 7)) {
         char shape_text[128];
         const char *a = spec + 7, *b = strchr(a, ':');
@@ -192,7 +192,7 @@ int qwen_serve_main(int argc, char **argv) {
     QwenCheckpoint checkpoint;
     int have_checkpoint = 0;
     char error[256];
-    if (open_model(&model, argv[2], 0, error, sizeof(error))) {
+    if (qwen_model_open(&model, argv[2], 0, error, sizeof(error))) {
         fprintf(stderr, "%s\n", error);
         return 2;
     }
@@ -396,7 +396,7 @@ int qwen_bounded_serve_main(int argc, char **argv) {
     QwenSession session;
     Ring cache;
     char error[256];
-    if (open_model(&model, argv[2], profile, error, sizeof(error))) {
+    if (qwen_model_open(&model, argv[2], profile, error, sizeof(error))) {
         fprintf(stderr, "%s\n", error);
         return 2;
     }

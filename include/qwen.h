@@ -177,6 +177,20 @@ int qwen_push_batch(QwenSession **sessions, int n, const int *tokens);
  * it stay pushed. */
 int qwen_prefill(QwenSession *, const int *tokens, int n);
 
+/* B200 addition: a model from a TCM1LE bundle path (loaded in weight profile
+ * `profile`, as qwen_model_init after tcm_load) or from a seeded specification
+ * seeded:SHAPE:SEED:PROFILE (SHAPE "qwen2.5-1.5b", "qwen2.5-1.5b@LAYERS" or
+ * HIDDENxLAYERSxQHEADSxKVHEADSxHEADxINTERMEDIATExVOCABxPOSITIONS; PROFILE 0
+ * FP32 or 2 BF16 matrices; weights N(0, 0.02), norms 1, biases 0). 0, or -1
+ * with a message in error. */
+int qwen_model_open(QwenModel *, const char *spec, int profile, char *error, size_t capacity);
+
+/* B200 addition: the reference's timed single-session run (src/qwen.c:438-503),
+ * `tcm-cuda qwen MODEL --tokens-file F [--new-tokens N] [--context C]
+ * [--output P] [--first-logits P] [--checkpoint-test] [--trace-prefix P
+ * --trace-layer L [--trace-position T]]`, printing the tcm-qwen-run-v1 JSON. */
+int qwen_main(int argc, char **argv);
+
 /* B200 addition: tensor-parallel decode of one session over `world` GPUs (2, 4
  * or 8), one process per GPU, each with the whole model and its own copy of the
  * session (qwen_b200_tp_open/_connect/_close in include/qwen_b200.h, applied

@@ -175,3 +175,65 @@ def test_bounded_protocol_replay_against_reference_serve():
     script = ["A " + prompt(9, 8), "G 3", "S", "P", "A 5 6", "S", "B 1", "S", "Q"]
     replay_matches("seeded:qwen2.5-1.5b:22:0", script, "--cache-policy", "bounded", "--context", "64", "--anchors",
                    "2", "--recent", "4", "--reservoir", "3")
+
+
+CPU_HOST_EXE = ROOT / "oracle" / "_ref" / "tcm-cuda-cpu"
+
+
+def qwen_run(exe, model, prompt_tokens, tmp_path, tag, *extra):
+    tokens = tmp_path / f"{tag}.txt"
+    tokens.write_text(" ".join(map(str, prompt_tokens)) + "\n")
+    proc = subprocess.run([str(exe), "qwen", model, "--tokens-file", str(tokens), "--output", str(tmp_path / f"{tag}.json"),
+                           "--first-logits", str(tmp_path / f"{tag}.f32"), *extra], capture_output=True, text=True,
+                          timeout=900)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    return json.loads((tmp_path / f"{tag}.json").read_text()), np.fromfile(tmp_path / f"{tag}.f32", np.float32)
+
+
+@pytest.mark.parametrize("profile,n_prompt,tol", [(0, 6, 1e-3), (2, 100, 3e-2)], ids=["fp32", "bf16-prefill"])
+def test_qwen_run_against_oracle(tmp_path, profile, n_prompt, tol):
+    """`tcm-cuda qwen` on the B200 (2-layer seeded model of Qwen2.5-1.5B widths):
+    the first-logits dump and every generated token against the oracle, and the
+    checkpoint test's exact replay. The BF16 prompt runs through the batched
+    prefill."""
+    from checkers import ORACLE, CpuDecoder
+    prompt_ids = [int(t) for t in np.random.default_rng(31).integers(0, 151936, n_prompt)]
+    run, first = qwen_run(SERVE, f"seeded:qwen2.5-1.5b@2:23:{profile}", prompt_ids, tmp_path, "gpu", "--new-tokens",
+                          "5", "--context", "128", "--checkpoint-test")
+    assert run["checkpoint_exact"] is True and run["generated_tokens"] == 5
+    law = cm.FillLaw(cm.Fill(0.0, 0.02), cm.Fill(1.0, 0.0), cm.Fill(0.0, 0.0))
+    o = CpuDecoder(ORACLE, cm.qwen_shape(2, 32768), 23, law, profile == 2, 128)
+    try:
+        for i, t in enumerate(prompt_ids):
+            top, logits = o.push(t, readout=i == len(prompt_ids) - 1)
+        assert float(np.max(np.abs(first - logits))) <= tol
+        for step in run["tokens"]:
+            if top[2] - top[3] > 2 * tol:
+                assert step["id"] == top[0]
+            assert abs(step["logit"] - top[2]) <= tol
+            top, _ = o.push(step["id"])
+    finally:
+        o.close()
+
+
+@pytest.mark.skipif(not CPU_HOST_EXE.exists(), reason="CPU host build absent")
+def test_qwen_run_port_trace_against_cpu_host(tmp_path):
+    """--trace-prefix/--trace-layer/--trace-position on the B200: the same 14
+    ports, in the same order and sizes, as the session host over the
+    reference's CPU primitives, and values within the FP32 bound."""
+    prompt_ids = [5, 77, 1234, 99, 42, 7]
+    args = ["--new-tokens", "3", "--context", "64", "--trace-layer", "1", "--trace-position", "4"]
+    gpu, _ = qwen_run(SERVE, "seeded:qwen2.5-1.5b@2:24:0", prompt_ids, tmp_path, "gpu", "--trace-prefix",
+                      str(tmp_path / "g"), *args)
+    cpu, _ = qwen_run(CPU_HOST_EXE, "seeded:qwen2.5-1.5b@2:24:0", prompt_ids, tmp_path, "cpu", "--trace-prefix",
+                      str(tmp_path / "c"), *args)
+    assert gpu["trace_ports"] == cpu["trace_ports"] == 14
+    lg = [json.loads(l) for l in (tmp_path / "g.jsonl").read_text().splitlines()]
+    lc = [json.loads(l) for l in (tmp_path / "c.jsonl").read_text().splitlines()]
+    assert lg == lc
+    for e in lg:
+        name = f"-{e['occurrence']:04d}-{e['port']}.f32"
+        a, b = np.fromfile(str(tmp_path / "g") + name, np.float32), np.fromfile(str(tmp_path / "c") + name, np.float32)
+        assert a.size == b.size == e["count"]
+        assert float(np.max(np.abs(a - b))) <= 1e-3 * max(1.0, float(np.max(np.abs(b))))
+    assert [t["id"] for t in gpu["tokens"]] == [t["id"] for t in cpu["tokens"]]
