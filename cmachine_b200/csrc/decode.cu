@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
         ring_release(ring, g);
     }
     trace_mark(a.trace, 3);
-    if (group) __threadfence_system();  // the logits reach every rank before this rank's top-2 flag
+    if (group && lane < a.tp.world) __threadfence_system();  // this lane's logits stores reach their rank first
     // Warp results (identical in every lane) -> CTA result -> last CTA merges.
     if (lane == 0) {
         sv[2 * warp] = t.a; sv[2 * warp + 1] = t.b;
