@@ -390,8 +390,7 @@ __device__ __forceinline__ void flash_rows(const Rows &rows, int r0, int r1, con
 template <int G, class Rows>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     Rows rows, const float *__restrict__ q, float inv_sqrt_dim, float *__restrict__ part,
-    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace, int defer,
-    Pace pace) {
+    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace, int defer) {
     static_assert(G <= 8, "query heads per KV head are padded to eight");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
@@ -419,7 +418,6 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     if (!multi && cid > 0) {  // whole clusters leave together
         pdl_trigger();
         if (mark && tid == 0) mark[0] = 0ull;  // no work: not part of the timeline
-        if (tid == 0) pace_signal(pace);
         return;
     }
     // First phase of a cluster barrier, waited on just before the first
@@ -449,7 +447,6 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
         }
         __syncthreads();
         if (tid == 0) {
-            pace_wait(pace);
             const uint32_t nb = (uint32_t)(rows.s1 - rows.s0) * kHeadDim * sizeof(float);
             if (nb) {
                 mbar_expect_tx(&kv_bar, 2 * nb);
@@ -484,7 +481,6 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     float *q_s = &wacc[0][0][0];
     if (tid < G * kHeadDim / 4) reinterpret_cast<float4 *>(q_s)[tid] = qpiece;
     __syncthreads();
-    if (tid == 0) pace_signal(pace);
 
     float4 q4[G], acc[G];
 #pragma unroll

@@ -41,7 +41,6 @@ struct QkvArgs {
     float *x, *q, *k, *v, *kcache, *vcache;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
-    Pace pace;                  // launch pacing (whole-token graph only)
     int qheads, kvheads, capacity;
     float eps;
 };
@@ -75,11 +74,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            pace_wait(a.pace);
+        if (lane == 0)
             ring_produce(ring, items, R, kRow<WT>, [&](int i) { int kd, hl, d; return (const void *)locate(i, kd, hl, d); },
                          &a.st->fault);
-        }
         return;
     }
     // Constants first (they do not depend on earlier kernels).
@@ -105,7 +102,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qkv_kernel(QkvArgs a) {
     if (!a.embed) load_lane_vec<WT>(xr, x_s, lane);
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     trace_mark(a.trace, 2);
-    if (threadIdx.x == 0) pace_signal(a.pace);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
         const int n = min(R, items - g * R);
@@ -161,7 +157,6 @@ struct ORowsArgs {
     float *x;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
-    Pace pace;                  // launch pacing (whole-token graph only)
     int group;           // query heads per KV head
 };
 // The deferred end of attn_decode_kernel: outputs o = threadIdx.x + 256 k
@@ -242,11 +237,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            pace_wait(a.pace);
+        if (lane == 0)
             ring_produce(ring, items, R, kRow<WT>, [&](int i) { return (const void *)(w + (size_t)(r0 + i) * kHidden); },
                          &a.st->fault);
-        }
         return;
     }
     pdl_wait();
@@ -260,7 +253,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
         for (int i = threadIdx.x; i < kHidden / 4; i += kConsumerWarps * 32)
             reinterpret_cast<float4 *>(a.in)[i] = reinterpret_cast<const float4 *>(in_s)[i];
     trace_mark(a.trace, 2);
-    if (threadIdx.x == 0) pace_signal(a.pace);
     const int groups = (items + R - 1) / R;
     for (int g = 0; g < groups; g++) {
         if (!ring_acquire(ring, g, &a.st->fault)) break;
@@ -286,7 +278,6 @@ struct GateUpArgs {
     float *h;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
-    Pace pace;                  // launch pacing (whole-token graph only)
     unsigned *sched;            // row-group counter of this launch site
     float eps;
     int inter;                  // intermediate units of this rank (all 8960 on one GPU)
@@ -308,12 +299,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            pace_wait(a.pace);
+        if (lane == 0)
             ring_produce_dynamic(ring, items, R, kRow<WT>,
                                  [&](int i) { return (const void *)((i & 1 ? wu : wg) + (size_t)(i >> 1) * kHidden); },
                                  a.sched, hdr_s, &a.st->fault);
-        }
         return;
     }
     stage_norm(nw_s, a.norm);
@@ -325,7 +314,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gateup_kernel(GateUpArgs a)
     load_lane_vec<WT>(xr, x_s, lane);
     rms_lane<WT>(xr, nw_s, a.eps, lane);
     trace_mark(a.trace, 2);
-    if (threadIdx.x == 0) pace_signal(a.pace);
     for (int g = 0;; g++) {
         bool failed = false;
         const int grp = ring_next(ring, g, hdr_s, &a.st->fault, &failed);
@@ -361,7 +349,6 @@ struct DownArgs {
     float *x;
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
-    Pace pace;                  // launch pacing (whole-token graph only)
     TpLink tp;                  // world 1: the sums go straight into the residual
     int layer;
 };
@@ -401,11 +388,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            pace_wait(a.pace);
+        if (lane == 0)
             ring_produce(ring, items, RD, G::kRowBytes, [&](int i) { return (const void *)(w + (size_t)(r0 + i) * kInter); },
                          &a.st->fault);
-        }
         return;
     }
     pdl_wait();
@@ -425,7 +410,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
         }
     }
     trace_mark(a.trace, 2);
-    if (threadIdx.x == 0) pace_signal(a.pace);
     constexpr bool group = SH > 1;  // a rank reads part of each row only inside a group
     const unsigned token = group ? __ldcg(a.tp.epoch) + 1u : 0u;
     const int groups = (items + RD - 1) / RD;
@@ -492,13 +476,11 @@ struct ReadoutArgs {
     unsigned *sync;  // [0] block counter, [1] non-finite flag
     DecodeState *st;
     unsigned long long *trace;  // per-CTA timestamps of this launch, or null
-    Pace pace;                  // launch pacing (whole-token graph only)
     TcmTop2 *log;
     unsigned *sched;            // row-group counter of this launch site
     int vocab;
     float eps;
     TpLink tp;                  // world > 1: this rank's vocabulary rows, logits to every rank, top-2 exchange
-    unsigned *pace_tok;         // advanced once per token when the launches are paced, or null
 };
 template <typename WT>
 __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs a) {
@@ -517,11 +499,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     trace_mark(a.trace, 0);
     pdl_trigger();
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            pace_wait(a.pace);
+        if (lane == 0)
             ring_produce_dynamic(ring, items, R, kRow<WT>, [&](int i) { return (const void *)(e + (size_t)i * kHidden); },
                                  a.sched, hdr_s, &a.st->fault);
-        }
         return;
     }
     stage_norm(nw_s, a.norm);
@@ -535,7 +515,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
     Top2 t = top2_empty();
     bool bad = false;
     trace_mark(a.trace, 2);
-    if (threadIdx.x == 0) pace_signal(a.pace);
     for (int g = 0;; g++) {
         bool failed = false;
         const int grp = ring_next(ring, g, hdr_s, &a.st->fault, &failed);
@@ -636,7 +615,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) readout_kernel(ReadoutArgs 
             st->invalid |= (int)flag;
             a.log[st->step % kLogCap] = top;
             st->step += 1;
-            if (a.pace_tok) *a.pace_tok += 1u;
             st->token = z.ai;
             st->position += 1;
             a.sync[0] = 0u;
@@ -738,8 +716,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) ring_selfcheck_kernel(SelfC
 
 // Token state from kernel arguments: nothing in host memory is read after the
 // launch call returns, so chained enqueues never race a host buffer.
-__global__ void set_state_kernel(DecodeState *st, int token, int position, unsigned *pace, int pace_words) {
-    for (int i = 0; i < pace_words; i++) pace[i] = 0u;
+__global__ void set_state_kernel(DecodeState *st, int token, int position) {
     st->token = token;
     st->position = position;
     st->step = 0;
@@ -813,11 +790,6 @@ struct QwenB200Runner {
     unsigned char *tp_area;     // this rank's exchange area (gpu_alloc, exported)
     void *tp_peer_area[kTpMax], *tp_peer_logits[kTpMax];  // opened peer mappings
     int tp_rank, tp_world;
-    // Launch pacing of the whole-token graph (stream.cuh Pace): one counter per
-    // launch site (layer * 5 + stage) and the tokens run since they were cleared.
-    unsigned *pace;
-    bool pacing;                // set while the whole-token graph is captured
-    bool pace_on;               // qwen_b200_tune key 0 (default on)
 };
 
 int tcm::decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
@@ -869,26 +841,6 @@ unsigned long long *trace_slot(QwenB200Runner *r) {
 }
 
 bool has_dense(const QwenB200Runner *r, int layer) { return r->slots[layer] >= 0; }
-// Pacing words: one counter per launch site (layer * 5 + stage), then the token count.
-int pace_words(const QwenB200Runner *r) { return r->d->s.layers * 5 + 1; }
-unsigned *pace_tok(const QwenB200Runner *r) { return r->pace + r->d->s.layers * 5; }
-// The pacing of stage `stage` (0 q/k/v .. 4 down, 5 readout) of `layer` inside
-// the whole-token graph: wait for the launch before it, count this one.
-Pace pace_of(const QwenB200Runner *r, int layer, int stage) {
-    Pace p = {};
-    if (!r->pacing) return p;
-    const int attention_ctas = kCluster * kClustersPerHead * r->d->s.kvheads;
-    p.tok = pace_tok(r);
-    if (stage < 5) p.signal = r->pace + layer * 5 + stage;
-    if (stage > 0) {
-        p.wait = r->pace + layer * 5 + (stage - 1);
-        p.expect = stage - 1 == 1 ? attention_ctas : r->grid;
-    } else if (layer > 0) {
-        p.wait = r->pace + (layer - 1) * 5 + 4;
-        p.expect = r->grid;
-    }
-    return p;
-}
 // The counter pair of a launch site. A kernel takes row groups from its pair
 // before its dependency wait, so no two launches of one token may share one.
 unsigned *sched_slot(const QwenB200Runner *r, int layer, int stage) { return r->sched + 2 * (layer * 5 + stage); }
@@ -911,14 +863,12 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.st = r->st;
     a.qheads = s.qheads; a.kvheads = s.kvheads; a.capacity = r->b.capacity; a.eps = s.epsilon;
     a.trace = trace_slot(r);
-    a.pace = pace_of(r, layer, 0);
     launch(qkv_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
 }
 // defer: leave the cluster partials in attn_part for the O projection to fold
 // (out is then written by that launch).
 template <class Rows>
-void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl, bool defer,
-                           Pace pace) {
+void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl, bool defer) {
     const QwenB200Shape &s = r->d->s;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCluster * kClustersPerHead, s.kvheads);
@@ -936,7 +886,7 @@ void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, 
     cfg.numAttrs = pdl ? 2 : 1;
     TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6, Rows>, rows, q, 1.0f / sqrtf((float)kHeadDim),
                                 r->attn_part, r->attn_counters, out, trace_slot(r),
-                                defer ? 1 : 0, pace));
+                                defer ? 1 : 0));
 }
 void launch_attention(QwenB200Runner *r, int layer, bool pdl, bool defer = false) {
     DenseRows rows = {};
@@ -945,7 +895,7 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl, bool defer = false
     rows.capacity = r->b.capacity;
     rows.position = &r->st->position;
     rows.fault = &r->st->fault;
-    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl, defer, pace_of(r, layer, 1));
+    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl, defer);
 }
 void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const float *k, const float *v, float *out,
                            bool pdl, bool defer = false) {
@@ -959,7 +909,7 @@ void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const f
     rows.kcur = k;
     rows.vcur = v;
     rows.invalid = &r->st->invalid;
-    launch_attention_rows(r, rows, q, out, pdl, defer, pace_of(r, layer, 1));
+    launch_attention_rows(r, rows, q, out, pdl, defer);
 }
 void launch_ring_cut(QwenB200Runner *r, const DecodeState *st, int write_slot, int sample_slot, int mode, bool logits,
                      bool pdl) {
@@ -972,7 +922,7 @@ void launch_ring_cut(QwenB200Runner *r, const DecodeState *st, int write_slot, i
 template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl, bool fold = false) {
     const QwenB200Shape &s = r->d->s;
     ORowsArgs o = {r->d->layers[layer].o, r->b.attention, fold ? r->attn_part : nullptr, r->b.x, r->st, trace_slot(r),
-                   pace_of(r, layer, 2), s.qheads / s.kvheads};
+                   s.qheads / s.kvheads};
     launch(oproj_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
 }
 // The link the launches of a runner carry (world 1 when no group is connected).
@@ -989,13 +939,13 @@ template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl
     const TpLink t = tp_link(r);
     const size_t first = (size_t)t.rank * t.inter * kHidden;  // this rank's first unit
     GateUpArgs g = {(const WT *)L.gate + first, (const WT *)L.up + first, L.post_norm, r->b.x, r->b.gate, r->st,
-                    trace_slot(r), pace_of(r, layer, 3), sched_slot(r, layer, 3), r->d->s.epsilon, t.inter};
+                    trace_slot(r), sched_slot(r, layer, 3), r->d->s.epsilon, t.inter};
     launch(gateup_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
 }
 template <typename WT, int SH> void launch_down_sh(QwenB200Runner *r, int layer, bool pdl) {
     const TpLink t = tp_link(r);
     DownArgs dn = {(const WT *)r->d->layers[layer].down + (size_t)t.rank * t.inter, r->b.gate, r->b.x, r->st,
-                   trace_slot(r), pace_of(r, layer, 4), t, layer};
+                   trace_slot(r), t, layer};
     launch(down_kernel<WT, SH>, dim3(r->grid), dim3(kStreamThreads),
            ring_smem_bytes(kDownStages, DownGeo<WT, SH>::kStageBytes), stream(), pdl, dn);
 }
@@ -1015,8 +965,7 @@ template <typename WT> void launch_mlp(QwenB200Runner *r, int layer, bool pdl, b
 template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
     const QwenB200Decoder *d = r->d;
     ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, trace_slot(r),
-                     pace_of(r, d->s.layers - 1, 5), r->log, sched_slot(r, d->s.layers, 0), d->s.vocab, d->s.epsilon,
-                     tp_link(r), r->pacing ? pace_tok(r) : nullptr};
+                     r->log, sched_slot(r, d->s.layers, 0), d->s.vocab, d->s.epsilon, tp_link(r)};
     launch(readout_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
            a);
 }
@@ -1036,10 +985,8 @@ void launch_finish(QwenB200Runner *r, bool pdl) {
     else launch_readout<float>(r, pdl);
 }
 void launch_token(QwenB200Runner *r) {
-    r->pacing = r->pace_on;  // only a whole token signals and waits on every launch site exactly once
     for (int l = 0; l < r->d->s.layers; l++) launch_layer(r, l, l > 0);
     launch_finish(r, true);
-    r->pacing = false;
 }
 
 bool all_dense(const QwenB200Runner *r) {
@@ -1130,7 +1077,6 @@ void write_state(QwenB200Runner *r, int token, int position) {
     // With a ring the whole state goes (the step follows the top-2 field).
     const size_t bytes = r->ring_on ? sizeof(DecodeState) : 8 * sizeof(int);
     TCM_CUDA(cudaMemcpyAsync(r->st, r->host, bytes, cudaMemcpyHostToDevice, stream()));
-    TCM_CUDA(cudaMemsetAsync(r->pace, 0, (size_t)pace_words(r) * sizeof(unsigned), stream()));
     r->after_host = true;
 }
 // Opens a token: the state, and with a ring the token cut (row store, sample
@@ -1223,9 +1169,6 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     const size_t sched_bytes = (size_t)(d->s.layers * 5 + 1) * 2 * sizeof(unsigned);
     r->sched = (unsigned *)gpu_alloc(sched_bytes);
     gpu_zero(r->sched, sched_bytes);
-    r->pace_on = true;
-    r->pace = (unsigned *)gpu_alloc((size_t)pace_words(r) * sizeof(unsigned));
-    gpu_zero(r->pace, (size_t)pace_words(r) * sizeof(unsigned));
     TCM_CUDA(cudaMallocHost((void **)&r->host, sizeof(DecodeState)));
     TCM_CUDA(cudaMallocHost((void **)&r->host_log, kLogCap * sizeof(TcmTop2)));
     r->launches = d->s.layers * 5 + 1;
@@ -1258,7 +1201,6 @@ void qwen_b200_runner_free(QwenB200Runner *r) {
     gpu_free(r->top_pi);
     gpu_free(r->sync);
     gpu_free(r->sched);
-    gpu_free(r->pace);
     gpu_free(r->pers_layers);
     gpu_free(r->pers_part);
     TCM_CUDA(cudaFreeHost(r->host));
@@ -1369,7 +1311,7 @@ int qwen_b200_enqueue(QwenB200Runner *r, int token, int position, int n) {
     if (!r || r->ring_on || n < 1 || n > kLogCap || !valid_token(r, token, position) || position + n > r->b.capacity ||
         (!use_persistent(r) && ensure_graph(r)))
         return -1;
-    set_state_kernel<<<1, 1, 0, stream()>>>(r->st, token, position, r->pace, pace_words(r));
+    set_state_kernel<<<1, 1, 0, stream()>>>(r->st, token, position);
     TCM_CUDA(cudaGetLastError());
     r->after_host = true;
     for (int i = 0; i < n; i++) run_token(r);
@@ -1390,16 +1332,6 @@ int qwen_b200_generate(QwenB200Runner *r, int token, int position, int n, int *i
 }
 
 int qwen_b200_launches_per_token(const QwenB200Runner *r) { return r ? (use_persistent(r) ? 1 : r->launches) : 0; }
-
-int qwen_b200_tune(QwenB200Runner *r, int key, int value) {
-    if (!r || key != 0 || (value != 0 && value != 1)) return -1;
-    TCM_CUDA(cudaStreamSynchronize(stream()));
-    if (r->pace_on != (value == 1)) {
-        r->pace_on = value == 1;
-        drop_graphs(r);
-    }
-    return 0;
-}
 
 int qwen_b200_persistent_tune(QwenB200Runner *r, int key, int value) {
     if (!r || key != 0 || value < 0 || value > 2048) return -1;
@@ -1463,14 +1395,14 @@ float qwen_b200_time_stage(QwenB200Runner *r, int stage, int layer, int position
         }
     };
     // The readout advances the device position; each launch restarts it.
-    set_state_kernel<<<1, 1, 0, stream()>>>(r->st, 0, position, r->pace, pace_words(r));
+    set_state_kernel<<<1, 1, 0, stream()>>>(r->st, 0, position);
     once(false);
     cudaEvent_t a, b;
     TCM_CUDA(cudaEventCreate(&a));
     TCM_CUDA(cudaEventCreate(&b));
     float total = 0.f;
     for (int i = 0; i < reps; i++) {
-        set_state_kernel<<<1, 1, 0, stream()>>>(r->st, 0, position, r->pace, pace_words(r));
+        set_state_kernel<<<1, 1, 0, stream()>>>(r->st, 0, position);
         TCM_CUDA(cudaEventRecord(a, stream()));
         once(false);
         TCM_CUDA(cudaEventRecord(b, stream()));

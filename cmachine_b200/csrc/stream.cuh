@@ -77,32 +77,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
         }
     }
 }
-// Pacing between consecutive launches of a whole-token graph, a timing hint
-// and never a correctness dependency. When a kernel is released, the next
-// kernel's CTAs take the SM slots the finished kernel left and start their
-// weight prefetch at once; that burst (up to ~15 MB) would sit in the memory
-// queues ahead of the released kernel's small input-vector loads. So each
-// kernel's thread 0 counts its CTA in `signal` once its input is loaded, and
-// the next kernel's producer waits (at most kPaceLimitNs) until every CTA of
-// the previous launch has done so before its first copy. Counters only grow:
-// the target is (tokens run since they were cleared + 1) x the previous
-// launch's CTAs; the host clears them with the token state.
-struct Pace {
-    const unsigned *wait;  // the previous launch's counter, or null (start at once)
-    unsigned *signal;      // this launch's counter, or null
-    const unsigned *tok;   // whole tokens run since the counters were cleared
-    unsigned expect;       // CTAs of the previous launch
-};
-constexpr unsigned long long kPaceLimitNs = 20000ull;  // 20 us
-__device__ __forceinline__ void pace_wait(const Pace &p) {
-    if (!p.wait) return;
-    const unsigned target = (*(const volatile unsigned *)p.tok + 1u) * p.expect;
-    const unsigned long long start = global_ns();
-    while ((int)(*(const volatile unsigned *)p.wait - target) < 0 && global_ns() - start < kPaceLimitNs) __nanosleep(32);
-}
-__device__ __forceinline__ void pace_signal(const Pace &p) {
-    if (p.signal) atomicAdd(p.signal, 1u);
-}
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte
 // aligned) completing a transaction on `bar`. No multicast.
 __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -253,13 +253,6 @@ int qwen_b200_tp_world(const QwenB200Runner *);
 int qwen_b200_wait_limit(unsigned long long ns);
 int qwen_b200_pipeline_check(const float *w, int rows, const float *x, float *y, int starve);
 
-/* Tuning of the whole-token graph: key 0 = launch pacing (1, the default: each
- * kernel's weight prefetch waits, at most 20 us, until the launch before it has
- * loaded its input vector, so that burst does not queue ahead of those loads;
- * 0: prefetch at once). Same bits either way. Returns 0, or -1 for an unknown
- * key or value. */
-int qwen_b200_tune(QwenB200Runner *, int key, int value);
-
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Whole-token execution: 1 = one persistent cooperative launch per token (one
