@@ -159,7 +159,6 @@ def _declare(L, strict: bool = True):
         "qwen_b200_launches_per_token": (c_int, [P]),
         "qwen_b200_persistent": (c_int, [P, c_int]),
         "qwen_b200_persistent_tune": (c_int, [P, c_int, c_int]),
-        "qwen_b200_tune": (c_int, [P, c_int, c_int]),
         "qwen_b200_time_stage": (c_float, [P, c_int, c_int, c_int, c_int]),
         "qwen_b200_trace": (c_int, [P, c_int]),
         "qwen_b200_trace_read": (c_int, [P, P, c_size_t]),

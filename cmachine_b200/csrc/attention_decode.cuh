@@ -387,20 +387,10 @@ __device__ __forceinline__ void flash_rows(const Rows &rows, int r0, int r1, con
     }
 }
 
-// Weight rows a later kernel of the layer streams first (the gate/up GEMV's
-// first row groups: the first rows of gate and of up), prefetched into L2 by
-// the attention CTAs at entry while the memory system is otherwise idle in the
-// layer's latency chain. bytes == 0: none. Every CTA takes an equal slice.
-struct AheadL2 {
-    const void *a, *b;
-    size_t bytes;  // of each range (a multiple of 16)
-};
-
 template <int G, class Rows>
 __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     Rows rows, const float *__restrict__ q, float inv_sqrt_dim, float *__restrict__ part,
-    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace, int defer,
-    AheadL2 ahead) {
+    unsigned *__restrict__ counters, float *__restrict__ out, unsigned long long *__restrict__ trace, int defer) {
     static_assert(G <= 8, "query heads per KV head are padded to eight");
     __shared__ float wm[kDecodeAttnWarps][G], wl[kDecodeAttnWarps][G];
     __shared__ __align__(16) float wacc[kDecodeAttnWarps][G][kHeadDim];
@@ -416,12 +406,6 @@ __global__ void __launch_bounds__(kDecodeAttnThreads, 2) attn_decode_kernel(
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     unsigned long long *mark = trace ? trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
     if (mark && tid == 0) mark[0] = attn_clock();
-    if (ahead.bytes && tid == 0) {  // no dependency on earlier kernels: weights only
-        const size_t ctas = (size_t)gridDim.x * gridDim.y, c = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
-        const size_t b0 = (ahead.bytes * c / ctas) & ~(size_t)15, b1 = (ahead.bytes * (c + 1) / ctas) & ~(size_t)15;
-        prefetch_range_l2(ahead.a, b0, c + 1 == ctas ? ahead.bytes : b1);
-        prefetch_range_l2(ahead.b, b0, c + 1 == ctas ? ahead.bytes : b1);
-    }
     // The token state (position, ring step) is written before a token's first
     // kernel and the cache rows below the newest were written by earlier
     // tokens, so the row split and an L2 prefetch of those rows need not wait

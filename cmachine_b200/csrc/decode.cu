@@ -20,7 +20,6 @@
 #include "kernels.h"
 #include "../../include/qwen_b200.h"
 #include "../../include/tcm_seeded.h"
-#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -791,7 +790,6 @@ struct QwenB200Runner {
     unsigned char *tp_area;     // this rank's exchange area (gpu_alloc, exported)
     void *tp_peer_area[kTpMax], *tp_peer_logits[kTpMax];  // opened peer mappings
     int tp_rank, tp_world;
-    unsigned ahead_rows;        // gate/up rows the attention prefetches into L2 (qwen_b200_tune key 0)
 };
 
 int tcm::decoder_view(const QwenB200Decoder *d, QwenB200Shape *shape, const QwenB200Layer **layers, const void **embed,
@@ -870,8 +868,7 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
 // defer: leave the cluster partials in attn_part for the O projection to fold
 // (out is then written by that launch).
 template <class Rows>
-void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl, bool defer,
-                           AheadL2 ahead = AheadL2{}) {
+void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, float *out, bool pdl, bool defer) {
     const QwenB200Shape &s = r->d->s;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCluster * kClustersPerHead, s.kvheads);
@@ -889,11 +886,8 @@ void launch_attention_rows(QwenB200Runner *r, const Rows &rows, const float *q, 
     cfg.numAttrs = pdl ? 2 : 1;
     TCM_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<6, Rows>, rows, q, 1.0f / sqrtf((float)kHeadDim),
                                 r->attn_part, r->attn_counters, out, trace_slot(r),
-                                defer ? 1 : 0, ahead));
+                                defer ? 1 : 0));
 }
-// The first gate and up rows of this layer's gate/up launch (this rank's rows
-// in a tensor-parallel group), ahead_rows of each.
-AheadL2 ahead_of(const QwenB200Runner *r, int layer);
 void launch_attention(QwenB200Runner *r, int layer, bool pdl, bool defer = false) {
     DenseRows rows = {};
     rows.keys = r->b.keys + slot_offset(r, layer);
@@ -901,7 +895,7 @@ void launch_attention(QwenB200Runner *r, int layer, bool pdl, bool defer = false
     rows.capacity = r->b.capacity;
     rows.position = &r->st->position;
     rows.fault = &r->st->fault;
-    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl, defer, defer ? ahead_of(r, layer) : AheadL2{});
+    launch_attention_rows(r, rows, r->b.q, r->b.attention, pdl, defer);
 }
 void launch_ring_attention(QwenB200Runner *r, int layer, const float *q, const float *k, const float *v, float *out,
                            bool pdl, bool defer = false) {
@@ -939,18 +933,6 @@ TpLink tp_link(const QwenB200Runner *r) {
     t.inter = kInter;
     t.vocab_end = r->d->s.vocab;
     return t;
-}
-AheadL2 ahead_of(const QwenB200Runner *r, int layer) {
-    AheadL2 a = {};
-    const TpLink t = tp_link(r);
-    const unsigned rows = std::min<unsigned>(r->ahead_rows, (unsigned)t.inter);
-    if (!rows) return a;
-    const size_t es = r->d->dtype == 2 ? 2 : 4, first = (size_t)t.rank * t.inter * kHidden * es;
-    const QwenB200Layer &L = r->d->layers[layer];
-    a.a = (const unsigned char *)L.gate + first;
-    a.b = (const unsigned char *)L.up + first;
-    a.bytes = (size_t)rows * kHidden * es;
-    return a;
 }
 template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Layer &L = r->d->layers[layer];
@@ -1350,16 +1332,6 @@ int qwen_b200_generate(QwenB200Runner *r, int token, int position, int n, int *i
 }
 
 int qwen_b200_launches_per_token(const QwenB200Runner *r) { return r ? (use_persistent(r) ? 1 : r->launches) : 0; }
-
-int qwen_b200_tune(QwenB200Runner *r, int key, int value) {
-    if (!r || key != 0 || value < 0 || value > kInter) return -1;
-    TCM_CUDA(cudaStreamSynchronize(stream()));
-    if (r->ahead_rows != (unsigned)value) {
-        r->ahead_rows = (unsigned)value;
-        drop_graphs(r);
-    }
-    return 0;
-}
 
 int qwen_b200_persistent_tune(QwenB200Runner *r, int key, int value) {
     if (!r || key != 0 || value < 0 || value > 2048) return -1;

@@ -103,12 +103,6 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
-// Prefetch [base + begin, base + end) into L2 (begin/end 16-byte multiples) in
-// pieces of at most 64 KB; fire and forget.
-__device__ __forceinline__ void prefetch_range_l2(const void *base, size_t begin, size_t end) {
-    const unsigned char *p = static_cast<const unsigned char *>(base);
-    for (size_t o = begin; o < end; o += 65536) bulk_prefetch_l2(p + o, (uint32_t)min((size_t)65536, end - o));
-}
 // Named barrier among the consumer warps only (the producer warp never joins).
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
 

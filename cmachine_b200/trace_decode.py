@@ -68,7 +68,6 @@ def main():
     ap.add_argument("--mode", choices=["graph", "persistent"], default="persistent")
     ap.add_argument("--lookahead", type=int, default=-1, help="persistent kernel L2 prefetch distance (KB)")
     ap.add_argument("--time", type=int, default=0, help="then time this many chained greedy tokens (device time)")
-    ap.add_argument("--ahead", type=int, default=-1, help="gate/up rows the attention prefetches into L2 (tune key 0)")
     args = ap.parse_args()
     L = cm.lib()
     import os
@@ -88,8 +87,6 @@ def main():
     for i in range(args.prompt):
         assert s.push((i * 7919 + 11) % model.shape.vocab) == 0
     runner = s.runner
-    if args.ahead >= 0:
-        assert L.qwen_b200_tune(runner, 0, args.ahead) == 0
     persistent = s.persistent(1 if args.mode == "persistent" else 0) == 1
     if persistent and args.lookahead >= 0:
         assert L.qwen_b200_persistent_tune(runner, 0, args.lookahead) == 0

@@ -253,12 +253,6 @@ int qwen_b200_tp_world(const QwenB200Runner *);
 int qwen_b200_wait_limit(unsigned long long ns);
 int qwen_b200_pipeline_check(const float *w, int rows, const float *x, float *y, int starve);
 
-/* Tuning of the token's kernels: key 0 = how many rows of gate and of up (each;
- * 0..8960, default 0) the attention kernel of each layer asks L2 to prefetch
- * at its start, ahead of the gate/up GEMV that streams them first. Same bits
- * for every value. Returns 0, or -1 for an unknown key or value. */
-int qwen_b200_tune(QwenB200Runner *, int key, int value);
-
 /* Kernel launches one token issues (for launch accounting). */
 int qwen_b200_launches_per_token(const QwenB200Runner *);
 /* Whole-token execution: 1 = one persistent cooperative launch per token (one
