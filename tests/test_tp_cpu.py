@@ -64,3 +64,43 @@ def test_host_refuses_group_without_fused_runner():
     assert s.push(3) == 0  # still a working session
     s.free()
     model.free()
+
+
+@pytest.mark.parametrize("elem_bytes", [4, 2], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("shards", [1, 2, 4, 8])
+def test_down_projection_tiling_covers_every_column_once(elem_bytes, shards):
+    """The down kernel's geometry (csrc/decode.cu DownGeo): a rank reads
+    F = 8960 / shards columns of each row, RD rows a stage, and its eight
+    consumer warps split a stage into PIECES pieces per row or RPW rows per warp.
+    Every (row slot, column) of a stage must be read by exactly one warp and lane
+    step, every copy must be whole 16-byte vectors at 16-byte-aligned offsets,
+    and a stage must stay within the 35 KB the ring was sized for."""
+    inter, warps = 8960, 8
+    E = 16 // elem_bytes
+    RD_base = 1 if elem_bytes == 4 else 2
+    F = inter // shards
+    RD = RD_base * shards
+    PIECES = 1 if RD >= warps else warps // RD
+    RPW = RD // warps if RD >= warps else 1
+    NVP = F // E // PIECES
+    KV = (NVP + 31) // 32
+    assert F % (E * PIECES) == 0 and (F * elem_bytes) % 16 == 0
+    assert PIECES * RD == warps or RPW * warps == RD
+    assert RD * F * elem_bytes <= 35840
+    for rank in range(shards):
+        assert (rank * F * elem_bytes) % 16 == 0  # the column offset of this rank's copies
+    seen = {}
+    for warp in range(warps):
+        piece = warp % PIECES if PIECES > 1 else 0
+        for j in range(RPW):
+            slot = warp // PIECES if PIECES > 1 else warp + warps * j
+            for lane in range(32):
+                for k in range(KV):
+                    if lane + 32 * k < NVP:
+                        v = piece * NVP + lane + 32 * k
+                        for e in range(E):
+                            key = (slot, E * v + e)
+                            assert key not in seen
+                            seen[key] = warp
+    assert len(seen) == RD * F
+    assert all(0 <= s < RD and 0 <= c < F for s, c in seen)
