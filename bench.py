@@ -211,11 +211,8 @@ def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: 
     import ctypes
     import numpy as np
     import cmachine_b200 as cm
-    from checkers import ORACLE, REF_CPU, load
-    path, kind = (REF_CPU, "reference") if REF_CPU.exists() else (ORACLE, "port")
-    L = load(path)
-    shape = cm.qwen_shape(layers, 4096)
-    model = L.orc_model_create(ctypes.byref(shape), 2026, ctypes.byref(cm.BENCH_LAW), int(bf16))
+    L, model, kind = reference_model(layers, 2 if bf16 else 0, 2026)
+    shape = cm.qwen_shape(layers, 32768)
     n = threads or max(1, min(os.cpu_count() or 1, 32))
     per_token = 1.3 * layers / 28 + 0.05
     steps = max(2, int(seconds / max(per_token, 1e-3)) // 1)
@@ -245,7 +242,6 @@ def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: 
     for th in pool:
         th.join()
     wall = time.perf_counter() - t0
-    L.orc_model_free(model)
     total = sum(results)
     sample = (f"{n} threads x (2-token prompt + {steps} greedy decode steps, every push counted), {layers}-layer "
               f"{'BF16' if bf16 else 'FP32'} seeded model, one session per thread")
@@ -509,6 +505,18 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
         per_row = json.loads(tf.read_text()).get("batch_attn_bytes_per_row")
         traffic = int(per_row * sum(p + 1 for p in pos)) if per_row else None
     L.qwen_b200_batch_free(batch)
+    parity = None
+    if getattr(args, "ref_check", False) and world == 1:
+        # Session 0's next batched step at its own context, checked by the reference CPU path.
+        s0 = sessions[0]
+        v0 = s0.view()
+        kv = session_kv(s0, shape.layers)
+        assert cm.push_batch([s0], [v0.pending]) == 0
+        parity = {"max_abs_dlogit": reference_dlogit_at_context(shape.layers, cfg["profile"], 2026 + rank, kv,
+                                                                 v0.position, v0.pending, s0.logits()),
+                  "context_rows": v0.position, "session": 0,
+                  "checker": "reference CPU path given the session's K/V rows (seeded context rows and the "
+                             "decoded ones)"}
     for s in sessions:
         s.free()
     model.free()
@@ -544,7 +552,65 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
                           "frac": round(step_bytes / (ms_per_step * 1e6) / peak, 4)},
         "stage_ms_layer0": {k: round(v, 5) for k, v in stage.items()},
         "clocks": clocks,
+        **({"parity_at_context": parity} if parity else {}),
     }
+
+
+REF_MODEL = {}  # the CPU leg's model of the last (layers, profile, seed), kept for the next use
+
+
+def reference_model(layers: int, profile: int, seed: int):
+    """The CPU leg's seeded model (the reference's CPU path from oracle/_ref,
+    else the oracle restatement): (library, model, kind). Building a 28-layer
+    model takes most of a minute on the host, so the last one is kept for the
+    CPU-baseline timing and the parity check of the same configuration."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import ctypes
+    import cmachine_b200 as cm
+    from checkers import ORACLE, REF_CPU, load
+    key = (layers, profile, seed)
+    if key not in REF_MODEL:
+        for L, model, _ in REF_MODEL.values():
+            L.orc_model_free(model)
+        REF_MODEL.clear()
+        path, kind = (REF_CPU, "reference") if REF_CPU.exists() else (ORACLE, "port")
+        L = load(path)
+        shape = cm.qwen_shape(layers, 32768)
+        model = L.orc_model_create(ctypes.byref(shape), seed, ctypes.byref(cm.BENCH_LAW), int(profile == 2))
+        REF_MODEL[key] = (L, model, kind)
+    return REF_MODEL[key]
+
+
+def reference_dlogit_at_context(layers: int, profile: int, seed: int, kv, position: int, token: int, gpu_logits):
+    """Part of the CPU-baseline leg, as the checker: the reference's own CPU
+    path (oracle/_ref, else the oracle restatement) receives the GPU session's
+    K/V rows 0..position-1 of every layer (kv[layer][kind], [kvheads][position]
+    [head]), places its cursor there and pushes `token`, the token the GPU
+    session pushed at `position`; returns max |delta logit| against the GPU's
+    logits of that push. This checks the decode step at the workload's real
+    context without prefilling it on the CPU."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import ctypes
+    import numpy as np
+    import cmachine_b200 as cm
+    L, model, _ = reference_model(layers, profile, seed)
+    session = L.orc_session_create(model, position + 1)
+    try:
+        for layer in range(layers):
+            for kind in (0, 1):
+                rows = np.ascontiguousarray(kv[layer][kind], np.float32)
+                L.orc_write_kv(session, layer, kind, position, ctypes.c_void_p(rows.ctypes.data))
+        assert L.orc_set_cursor(session, position) == 0
+        top = cm.Top2()
+        logits = np.empty(gpu_logits.size, np.float32)
+        assert L.orc_push(session, token, ctypes.byref(top), ctypes.c_void_p(logits.ctypes.data)) == 0
+        return float(np.max(np.abs(gpu_logits - logits)))
+    finally:
+        L.orc_session_free(session)
+
+
+def session_kv(session, layers: int):
+    return [[session.kv(layer, kind) for kind in (0, 1)] for layer in range(layers)]
 
 
 def gpu_dlogit(layers: int, profile: int, ref_logits):
@@ -664,6 +730,15 @@ def run_b200(args, cfg, world, rank, local, dist, torch, tp=False):
     if tp:
         assert s.tp_close() == 0
         barrier(dist, torch)
+    parity = None
+    if getattr(args, "ref_check", False) and world == 1:
+        # The GPU's next token at the workload's context, checked by the reference CPU path.
+        assert s.restore(ckpt) == 0
+        kv = session_kv(s, shape.layers)
+        assert s.push(p0) == 0
+        parity = {"max_abs_dlogit": reference_dlogit_at_context(shape.layers, cfg["profile"], 2026 + salt, kv, pos0, p0,
+                                                                 s.logits()),
+                  "context_rows": pos0, "checker": "reference CPU path given the session's K/V rows"}
     s.free()
     model.free()
     traffic = None
@@ -700,6 +775,8 @@ def run_b200(args, cfg, world, rank, local, dist, torch, tp=False):
         "clocks": clocks,
         "last_top2": top.tuple(),
     }
+    if parity:
+        line["parity_at_context"] = parity
     return line
 
 
@@ -746,6 +823,7 @@ def main():
     global CLOCKS
     CLOCKS = ClockSampler(local).start()
     try:
+        args.ref_check = world == 1 and not args.no_cpu_baseline  # the CPU-baseline leg's checker, 1 GPU only
         line = run_workload(args, args.config, world, rank, local, dist, torch, cpu=not args.no_cpu_baseline)
         if args.config == DEFAULT_CONFIG and not args.no_extras:
             # The other configurations the metric names, measured in the same run:
@@ -757,6 +835,7 @@ def main():
                 strong = dict(CONFIGS["bf16-batch64"], strong=True, total=64)
                 line["bs64_strong"] = compact(run_batched(args, strong, world, rank, local, dist, torch))
             line["bf16_ctx4096"] = compact(run_workload(args, "bf16-ctx4096", world, rank, local, dist, torch))
+            args.ref_check = False
             line["bounded"] = compact(run_workload(args, "bf16-bounded", world, rank, local, dist, torch))
             if world > 1 and world in (2, 4, 8):
                 # Last, so that a failure here costs only this sub-line: one
