@@ -1,4 +1,4 @@
-"""Tensor-parallel decode of one session over two GPUs (one process each).
+"""Tensor-parallel decode of one session over 2, 4 or 8 GPUs (one process each).
 
 Each rank loads the same seeded model and opens the same session, exports its
 exchange handle, gathers the other's over a gloo process group, connects, and
@@ -9,7 +9,7 @@ decodes the same prompt and greedy continuation. Checked on every token:
     adds the partials in rank order on every rank);
   - against the same decode on one GPU within the same bounds (only the order
     of the down projection's sum differs).
-Needs two GPUs; skipped on a one-GPU box.
+Each world size runs where the box has that many GPUs and is skipped otherwise.
 """
 import os
 import sys
@@ -21,7 +21,6 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 ROOT = Path(__file__).resolve().parent.parent
-WORLD = 2
 
 
 def gpu_count():
@@ -93,15 +92,17 @@ def _rank(rank, world, port, profile, out):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(gpu_count() < WORLD, reason="tensor-parallel decode needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("profile", [0, 2], ids=["fp32", "bf16"])
-def test_tensor_parallel_two_gpus(profile):
+def test_tensor_parallel(profile, world):
+    if gpu_count() < world:
+        pytest.skip(f"tensor-parallel decode over {world} GPUs needs {world} GPUs")
     import torch.multiprocessing as mp
     tol = 1e-3 if profile == 0 else 3e-2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + profile
-    procs = [ctx.Process(target=_rank, args=(r, WORLD, port, profile, q)) for r in range(WORLD)]
+    port = 29700 + 10 * world + profile
+    procs = [ctx.Process(target=_rank, args=(r, world, port, profile, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = sorted((q.get(timeout=600) for _ in procs), key=lambda r: r["rank"])
@@ -111,9 +112,10 @@ def test_tensor_parallel_two_gpus(profile):
         assert "error" not in r, r
     for p in procs:
         assert p.exitcode == 0
-    a, b = results
-    assert a["digests"] == b["digests"], "ranks disagree on logits or top-2"
-    assert a["kv"] == b["kv"], "ranks disagree on K/V"
-    print(f"TP-2 profile {profile}: max|dlogit| vs oracle {a['worst_oracle']:.3e}, vs one GPU {a['worst_single']:.3e}")
+    a = results[0]
+    for b in results[1:]:
+        assert a["digests"] == b["digests"], f"ranks 0 and {b['rank']} disagree on logits or top-2"
+        assert a["kv"] == b["kv"], f"ranks 0 and {b['rank']} disagree on K/V"
+    print(f"TP-{world} profile {profile}: max|dlogit| vs oracle {a['worst_oracle']:.3e}, vs one GPU {a['worst_single']:.3e}")
     assert a["worst_oracle"] <= tol
     assert a["worst_single"] <= tol
