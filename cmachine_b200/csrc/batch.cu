@@ -119,7 +119,7 @@ struct SessionMeta {
 };
 __device__ __forceinline__ void stage_meta(const BatchState *st, unsigned char *scratch, int e) {
     SessionMeta *m = reinterpret_cast<SessionMeta *>(scratch);
-    for (int n = e; n < st->n; n += 128)
+    for (int n = e; n < st->n; n += kTcEpiThreads)
         m[n] = SessionMeta{st->keys[n], st->values[n], st->logits[n], st->position[n], st->capacity[n]};
 }
 static_assert(sizeof(SessionMeta) * kBN <= 2048, "epilogue scratch");
@@ -142,7 +142,7 @@ struct EpiQkv {
         const int kind = t < 12 ? 0 : (t < 14 ? 1 : 2), head = t < 12 ? t : (t < 14 ? t - 12 : t - 14);
         const float *bias = (kind == 0 ? bq : kind == 1 ? bk : bv) + head * 128;
         const int np = p1 - p0, n_active = st->n;
-        for (int idx = e; idx < np * n_active; idx += 128) {
+        for (int idx = e; idx < np * n_active; idx += kTcEpiThreads) {
             const int d = p0 + idx % np, n = idx / np;
             float y0 = __fadd_rn(tile[d][n], bias[d]), y1 = __fadd_rn(tile[d + 64][n], bias[d + 64]);
             const SessionMeta &mt = meta[n];
@@ -183,16 +183,16 @@ struct EpiResid {
     template <int NP>
     __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *) const {
         const int np = p1 - p0, total = 2 * np * st->n;
-        for (int base = 0; base < total; base += 128 * 8) {
+        for (int base = 0; base < total; base += kTcEpiThreads * 8) {
             float xv[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int i = base + e + 128 * j;
+                const int i = base + e + kTcEpiThreads * j;
                 xv[j] = i < total ? x[(size_t)(i / (2 * np)) * kHd + t * 128 + pair_row(i, p0, np)] : 0.f;
             }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int i = base + e + 128 * j;
+                const int i = base + e + kTcEpiThreads * j;
                 if (i < total) {
                     const int r = pair_row(i, p0, np), n = i / (2 * np);
                     x[(size_t)n * kHd + t * 128 + r] = __fadd_rn(xv[j], tile[r][n]);
@@ -211,7 +211,7 @@ struct EpiSwiglu {
     template <int NP>
     __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *) const {
         const int np = p1 - p0, n_active = st->n;
-        for (int idx = e; idx < np * n_active; idx += 128) {
+        for (int idx = e; idx < np * n_active; idx += kTcEpiThreads) {
             const int i = p0 + idx % np, n = idx / np;
             const float g = tile[i][n], u = tile[i + 64][n];
             const float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
@@ -231,7 +231,7 @@ struct EpiLogits {
     __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *scratch) const {
         const SessionMeta *meta = reinterpret_cast<const SessionMeta *>(scratch);
         const int np = p1 - p0, total = 2 * np * st->n;
-        for (int i = e; i < total; i += 128) {
+        for (int i = e; i < total; i += kTcEpiThreads) {
             const int r = pair_row(i, p0, np), n = i / (2 * np);
             meta[n].logits[t * 128 + r] = tile[r][n];
         }
@@ -247,7 +247,7 @@ struct EpiStore {
     template <int NP>
     __device__ void store(int t, const float (*tile)[NP], int p0, int p1, int e, unsigned char *) const {
         const int np = p1 - p0, total = 2 * np * n;
-        for (int i = e; i < total; i += 128) {
+        for (int i = e; i < total; i += kTcEpiThreads) {
             const int r = pair_row(i, p0, np), c = i / (2 * np);
             y[(size_t)c * rows + t * 128 + r] = tile[r][c];
         }

@@ -8,7 +8,7 @@
 // significant bits, so the product tracks the reference's BF16-weight x FP32
 // activation arithmetic to ~1e-5 relative instead of BF16's ~4e-3.
 //
-// One CTA per SM (persistent over work items), 6 warps:
+// One CTA per SM (persistent over work items), 10 warps:
 //   warp 0  producer: one thread issues TMA tile loads (W box 64 x 64 twice per
 //           stage for a 128-row tile, X hi and lo boxes 64 x N) into a ring of
 //           shared-memory stages in the 128-byte swizzle, each stage completing
@@ -18,10 +18,13 @@
 //           thread issues tcgen05.mma kind::f16 (M = 128, N, K = 16; four per
 //           64-wide k-block and operand half) and tcgen05.commit to release
 //           stages and publish accumulators;
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator (warp w reads lanes
-//           32 * (w % 4) ...), then either the tile's final values or, with
+//   warps 2-9 epilogue: tcgen05.ld of the accumulator (warp w reads lanes
+//           32 * (w % 4) ..., warps 2-5 the first half of the columns and
+//           warps 6-9 the second), then either the tile's final values or, with
 //           split K, a partial to global memory of which the last CTA to arrive
 //           sums the splits in order (deterministic) and finishes the tile.
+//           The epilogue's per-element work (folds, bias, RoPE, SwiGLU, BF16
+//           splits) is latency-bound, so two warps per scheduler run it.
 // With split K launched as thread-block clusters (one cluster of `splits` CTAs
 // per tile, one item per CTA), every CTA leaves its partial tile in shared
 // memory, and after a cluster barrier each rank folds its own slice of row
@@ -40,7 +43,8 @@
 
 namespace tcm {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcEpiThreads = 256;                 // warps 2-9
+constexpr int kTcThreads = 64 + kTcEpiThreads;
 constexpr int kTcKBlock = 64;  // BF16 elements per k-block (one 128-byte swizzle row)
 constexpr uint32_t kTcATile = 128 * 128;  // bytes: 128 rows x 64 BF16
 
@@ -98,8 +102,8 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
-// Epilogue warps only (128 threads, named barrier 2).
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+// Epilogue warps only (kTcEpiThreads threads, named barrier 2).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiThreads) : "memory"); }
 
 // The A source of output tile t: rows [r0, r0 + 64) of map m0 and rows
 // [r1, r1 + 64) of map m1 form the tile's 128 rows.
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_free[b], 128);
+            mbar_init(&acc_free[b], kTcEpiThreads);
         }
         mbar_fence_init();
     }
@@ -264,8 +268,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             tc_mark(a.trace, 3);
         }
     } else {
-        // Epilogue: 128 threads, thread e owns tile row e (tensor-memory lane).
-        const int e = (warp & 3) * 32 + lane;  // warps 2..5 -> lane quarters 2,3,0,1
+        // Epilogue: kTcEpiThreads threads. Thread e holds row rr of the tile
+        // (its tensor-memory lane) and the columns [c0, c0 + H) of its half.
+        constexpr int H = N / 2;
+        static_assert(H % 16 == 0, "each epilogue half reads whole 16-column loads");
+        const int e = (warp - 2) * 32 + lane;
+        const int rr = (warp & 3) * 32 + lane;  // warps 2..5 and 6..9 -> lane quarters 2,3,0,1
+        const int c0 = ((warp - 2) >> 2) * H;
         pdl_wait();
         if (e == 0) tc_mark(a.trace, 4);
         a.epi.init(scratch, e);
@@ -278,10 +287,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (!mbar_wait(&acc_full[buf], (local >> 1) & 1, a.err, kTcErrAcc)) break;
             tc_fence_after();
             if (e == 0 && local == 0) tc_mark(a.trace, 5);
-            float v[N];
-            const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * N);
+            float v[H];
+            const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * N + c0);
 #pragma unroll
-            for (int c = 0; c < N; c += 16) {
+            for (int c = 0; c < H; c += 16) {
                 float r[16];
                 tc_ld16(taddr + (uint32_t)c, r);
 #pragma unroll
@@ -293,15 +302,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 // Partial to this CTA's shared tile; the cluster folds it below.
                 epi_sync();
 #pragma unroll
-                for (int c = 0; c < N; c++) tile[e][c] = v[c];
+                for (int c = 0; c < H; c++) tile[rr][c0 + c] = v[c];
                 continue;
             }
             bool finish = true;
             if (a.splits > 1) {
                 const int split = item % a.splits;
-                float4 *p = reinterpret_cast<float4 *>(a.part + (((size_t)t * a.splits + split) * 128 + e) * N);
+                float4 *p = reinterpret_cast<float4 *>(a.part + (((size_t)t * a.splits + split) * 128 + rr) * N + c0);
 #pragma unroll
-                for (int c = 0; c < N; c += 4) p[c / 4] = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+                for (int c = 0; c < H; c += 4) p[c / 4] = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
                 __threadfence();
                 epi_sync();
                 if (e == 0) *flag = atomicAdd(&a.counters[t], 1u) == (unsigned)(a.splits - 1);
@@ -310,11 +319,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 if (finish) {
                     __threadfence();
 #pragma unroll
-                    for (int c = 0; c < N; c++) v[c] = 0.f;
+                    for (int c = 0; c < H; c++) v[c] = 0.f;
                     for (int sp = 0; sp < a.splits; sp++) {
-                        const float4 *q = reinterpret_cast<const float4 *>(a.part + (((size_t)t * a.splits + sp) * 128 + e) * N);
+                        const float4 *q =
+                            reinterpret_cast<const float4 *>(a.part + (((size_t)t * a.splits + sp) * 128 + rr) * N + c0);
 #pragma unroll
-                        for (int c = 0; c < N; c += 4) {
+                        for (int c = 0; c < H; c += 4) {
                             const float4 w = __ldcg(q + c / 4);
                             v[c] += w.x;
                             v[c + 1] += w.y;
@@ -328,7 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (finish) {
                 epi_sync();  // the previous tile's readers are done with `tile`
 #pragma unroll
-                for (int c = 0; c < N; c++) tile[e][c] = v[c];
+                for (int c = 0; c < H; c++) tile[rr][c0 + c] = v[c];
                 epi_sync();
                 a.epi.store(t, tile, 0, 64, e, scratch);
             }
@@ -350,25 +360,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         static_assert((size_t)150 * kRS * 4 <= (size_t)G::kStages * G::kStage, "cluster receive buffer");
         const int S = a.cluster, r = (int)cluster.block_rank(), t = blockIdx.x / S;
         const int npmax = (64 + S - 1) / S;
-        const int e = (warp & 3) * 32 + lane;
+        const int e = (warp - 2) * 32 + lane;  // epilogue thread (warps 2-9)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the ring's async-proxy use is over
         cluster.sync();
         if (warp >= 2) {
-            const int pr = e & 63, half = e >> 6;
+            // Thread e sends half ch of tile row e % 128 (row pair pr, upper or lower).
+            constexpr int H = N / 2;
+            const int row = e & 127, pr = row & 63, half = row >> 6, ch = e >> 7;
             int o = 0;
             while (o + 1 < S && (o + 1) * 64 / S <= pr) o++;
             const int op0 = o * 64 / S, onp = (o + 1) * 64 / S - op0;
             float *dst = cluster.map_shared_rank(reinterpret_cast<float *>(smem), o) +
-                         ((size_t)r * 2 * npmax + (pr - op0) + half * onp) * kRS;
+                         ((size_t)r * 2 * npmax + (pr - op0) + half * onp) * kRS + ch * H;
+            const float *src = &tile[row][ch * H];
 #pragma unroll
-            for (int c = 0; c < N; c += 4)
-                *reinterpret_cast<float4 *>(dst + c) = make_float4(tile[e][c], tile[e][c + 1], tile[e][c + 2], tile[e][c + 3]);
+            for (int c = 0; c < H; c += 4)
+                *reinterpret_cast<float4 *>(dst + c) = make_float4(src[c], src[c + 1], src[c + 2], src[c + 3]);
         }
         cluster.sync();  // every row has reached its owner
         if (warp >= 2) {
             const int p0 = r * 64 / S, p1 = (r + 1) * 64 / S, np = p1 - p0, count = 2 * np * N;
             const float *recv = reinterpret_cast<const float *>(smem);
-            for (int idx = e; idx < count; idx += 128) {
+            for (int idx = e; idx < count; idx += kTcEpiThreads) {
                 const int jr = idx / N, c = idx % N;
                 float part[16];  // all of the element's slices requested first
 #pragma unroll
