@@ -20,6 +20,7 @@
 #include "kernels.h"
 #include "../../include/qwen_b200.h"
 #include "../../include/tcm_seeded.h"
+#include <type_traits>
 #include <mutex>
 #include <vector>
 
@@ -832,7 +833,7 @@ void setup_kernels() {
     });
 }
 
-constexpr int kTraceLaunches = 160, kTraceCtas = 160;
+constexpr int kTraceLaunches = 160, kTraceCtas = 320;
 constexpr unsigned kDefaultLookahead = 0u;  // persistent kernel: L2 prefetch distance per CTA (measured: no gain)
 // The trace slot of the next launch (launch order within a token), or null.
 unsigned long long *trace_slot(QwenB200Runner *r) {
@@ -849,6 +850,17 @@ size_t slot_offset(const QwenB200Runner *r, int layer) {
     return (size_t)r->slots[layer] * s.kvheads * r->b.capacity * s.head;
 }
 
+// Streamed GEMV kernels launched with two CTAs per SM (each CTA's ring and
+// vectors take under half of an SM's shared memory), by kernel and weight
+// type: every BF16 kernel, and the FP32 down projection and readout. Two rings
+// per SM keep twice the weight bytes in flight; the FP32 q/k/v, O and gate/up
+// kernels measured slower that way.
+enum GemvKind { kGemvQkv, kGemvOproj, kGemvGateUp, kGemvDown, kGemvReadout };
+template <typename WT> constexpr bool gemv_wide(GemvKind k) {
+    return std::is_same<WT, uint16_t>::value || k == kGemvDown || k == kGemvReadout;
+}
+template <typename WT> int gemv_grid(const QwenB200Runner *r, GemvKind k) { return gemv_wide<WT>(k) ? 2 * r->grid : r->grid; }
+
 template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     const QwenB200Decoder *d = r->d;
     const QwenB200Shape &s = d->s;
@@ -863,7 +875,7 @@ template <typename WT> void launch_qkv(QwenB200Runner *r, int layer, bool pdl) {
     a.st = r->st;
     a.qheads = s.qheads; a.kvheads = s.kvheads; a.capacity = r->b.capacity; a.eps = s.epsilon;
     a.trace = trace_slot(r);
-    launch(qkv_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
+    launch(qkv_kernel<WT>, dim3(gemv_grid<WT>(r, kGemvQkv)), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, a);
 }
 // defer: leave the cluster partials in attn_part for the O projection to fold
 // (out is then written by that launch).
@@ -923,7 +935,7 @@ template <typename WT> void launch_oproj(QwenB200Runner *r, int layer, bool pdl,
     const QwenB200Shape &s = r->d->s;
     ORowsArgs o = {r->d->layers[layer].o, r->b.attention, fold ? r->attn_part : nullptr, r->b.x, r->st, trace_slot(r),
                    s.qheads / s.kvheads};
-    launch(oproj_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
+    launch(oproj_kernel<WT>, dim3(gemv_grid<WT>(r, kGemvOproj)), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, o);
 }
 // The link the launches of a runner carry (world 1 when no group is connected).
 TpLink tp_link(const QwenB200Runner *r) {
@@ -940,13 +952,13 @@ template <typename WT> void launch_gateup(QwenB200Runner *r, int layer, bool pdl
     const size_t first = (size_t)t.rank * t.inter * kHidden;  // this rank's first unit
     GateUpArgs g = {(const WT *)L.gate + first, (const WT *)L.up + first, L.post_norm, r->b.x, r->b.gate, r->st,
                     trace_slot(r), sched_slot(r, layer, 3), r->d->s.epsilon, t.inter};
-    launch(gateup_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
+    launch(gateup_kernel<WT>, dim3(gemv_grid<WT>(r, kGemvGateUp)), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl, g);
 }
 template <typename WT, int SH> void launch_down_sh(QwenB200Runner *r, int layer, bool pdl) {
     const TpLink t = tp_link(r);
     DownArgs dn = {(const WT *)r->d->layers[layer].down + (size_t)t.rank * t.inter, r->b.gate, r->b.x, r->st,
                    trace_slot(r), t, layer};
-    launch(down_kernel<WT, SH>, dim3(r->grid), dim3(kStreamThreads),
+    launch(down_kernel<WT, SH>, dim3(gemv_grid<WT>(r, kGemvDown)), dim3(kStreamThreads),
            ring_smem_bytes(kDownStages, DownGeo<WT, SH>::kStageBytes), stream(), pdl, dn);
 }
 template <typename WT> void launch_down(QwenB200Runner *r, int layer, bool pdl) {
@@ -966,7 +978,7 @@ template <typename WT> void launch_readout(QwenB200Runner *r, bool pdl) {
     const QwenB200Decoder *d = r->d;
     ReadoutArgs a = {d->embed, d->norm, r->b.x, r->b.logits, r->top_pv, r->top_pi, r->sync, r->st, trace_slot(r),
                      r->log, sched_slot(r, d->s.layers, 0), d->s.vocab, d->s.epsilon, tp_link(r)};
-    launch(readout_kernel<WT>, dim3(r->grid), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
+    launch(readout_kernel<WT>, dim3(gemv_grid<WT>(r, kGemvReadout)), dim3(kStreamThreads), ring_smem_bytes(kStages, kStage<WT>), stream(), pdl,
            a);
 }
 
@@ -1162,8 +1174,8 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->attn_counters = (unsigned *)gpu_alloc((size_t)d->s.kvheads * sizeof(unsigned));
     gpu_zero(r->attn_counters, (size_t)d->s.kvheads * sizeof(unsigned));
     r->grid = sm_count();
-    r->top_pv = (float *)gpu_alloc((size_t)2 * r->grid * sizeof(float));
-    r->top_pi = (int *)gpu_alloc((size_t)2 * r->grid * sizeof(int));
+    r->top_pv = (float *)gpu_alloc((size_t)4 * r->grid * sizeof(float));  // two per CTA, up to two CTAs per SM
+    r->top_pi = (int *)gpu_alloc((size_t)4 * r->grid * sizeof(int));
     r->sync = (unsigned *)gpu_alloc(2 * sizeof(unsigned));
     gpu_zero(r->sync, 2 * sizeof(unsigned));
     const size_t sched_bytes = (size_t)(d->s.layers * 5 + 1) * 2 * sizeof(unsigned);

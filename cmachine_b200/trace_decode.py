@@ -31,7 +31,7 @@ import numpy as np
 
 import cmachine_b200 as cm
 
-LAUNCHES, CTAS = 160, 160
+LAUNCHES, CTAS = 160, 320
 STAGES = ["qkv", "attention", "oproj", "gateup", "down"]
 PHASES = ["qkv", "attention", "merge", "oproj", "gateup", "down"]
 MARKS = 512
