@@ -15,7 +15,8 @@ positions 512..767 (each 256-step segment restarts from the post-prompt state).
 
 The default run adds, in the same JSON line, the other configurations the
 metric names, each a sub-object with its own value, e2e, roofline and clocks:
-  bs64          64 independent sessions per GPU (contexts 128..8192), batched
+  bs64          64 independent sessions per GPU (contexts 128..8192, each a
+                uniform-random prompt run through qwen_prefill, untimed), batched
                 tcgen05 decode; at N > 1 weak scaling (64 sessions per GPU);
   bs64_strong   N > 1 only: 64 sessions in all, dealt over the N GPUs;
   bf16_ctx4096  BF16 weights, 4096-token prompt, 512-token decode window;
@@ -417,24 +418,25 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
     if strong:  # one fixed set of `total` sessions, dealt round-robin over the ranks
         total = cfg["total"]
         every = np.random.default_rng(11).integers(cfg["ctx"][0], cfg["ctx"][1] + 1, total)
-        lengths = [int(v) for v in every[rank::world]]
+        ids = list(range(rank, total, world))
+        lengths = [int(every[i]) for i in ids]
         n = len(lengths)
-        rng = np.random.default_rng(1011 + rank)
     else:
         rng = np.random.default_rng(11 + rank)
         lengths = [int(v) for v in rng.integers(cfg["ctx"][0], cfg["ctx"][1] + 1, n)]
+        ids = [rank * n + i for i in range(n)]
     sessions = []
-    for i, ln in enumerate(lengths):
+    t_prefill = time.time()
+    for i, ln in zip(ids, lengths):
         s = cm.Session(model, ln + steps // 2 + seg + max(args.warmup, 3) + 2)
-        v = s.view()
-        count = shape.layers * shape.kvheads * v.capacity * shape.head
-        # The context's K/V rows: seeded synthetic values of the decoder's K/V
-        # scale (the decode steps themselves are computed exactly).
-        L.qwen_b200_seeded_fill(c_void_p(v.keys), 1, 4242 + rank, 100000 + 2 * i, count, 0.0, 0.8)
-        L.qwen_b200_seeded_fill(c_void_p(v.values), 1, 4242 + rank, 100001 + 2 * i, count, 0.0, 0.8)
-        assert L.qwen_b200_session_set_cursor(s.handle, ln, int(rng.integers(0, shape.vocab))) == 0
+        # The context: a uniform-random prompt of ln token ids (seeded per
+        # session), run through qwen_prefill (batched causal chunks of 64 tokens
+        # on the tensor cores), so every cached K/V row is the model's own.
+        prompt = np.random.default_rng(70000 + i).integers(0, shape.vocab, ln)
+        assert s.prefill(prompt) == 0
         sessions.append(s)
     L.gpu_sync()
+    prefill_s = time.time() - t_prefill
     batch = L.qwen_b200_batch_create(L.qwen_b200_model_decoder(model.handle))
     assert batch
     views = [s.view() for s in sessions]
@@ -515,8 +517,8 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
         parity = {"max_abs_dlogit": reference_dlogit_at_context(shape.layers, cfg["profile"], 2026 + rank, kv,
                                                                  v0.position, v0.pending, s0.logits()),
                   "context_rows": v0.position, "session": 0,
-                  "checker": "reference CPU path given the session's K/V rows (seeded context rows and the "
-                             "decoded ones)"}
+                  "checker": "reference CPU path given the session's K/V rows (the prefilled context and the "
+                             "decoded rows)"}
     for s in sessions:
         s.free()
     model.free()
@@ -531,7 +533,8 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
                    "context": "uniform 128..8192 per session (seeded)",
                    "mean_position": round(mean_pos, 1), "segment": seg,
                    "checkpoints": "every segment; rollback after every second segment",
-                   "kv_prefill": "context K/V rows are seeded synthetic values; decode steps exact",
+                   "kv_prefill": "uniform-random prompt of each session's context length through qwen_prefill "
+                                 "(untimed)", "prefill_s": round(prefill_s, 1),
                    "parallelism": f"replicas{world}", "weights": "seeded N(0,0.02) random init",
                    "l2": "inputs larger than L2 (weights and K/V stream from HBM every step)"},
         "e2e": {"value": round(e2e_steps * tokens_total / steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
