@@ -506,6 +506,7 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
     if tf.exists():  # ncu DRAM bytes per cache row (a 4,096-row capture), scaled to these rows
         per_row = json.loads(tf.read_text()).get("batch_attn_bytes_per_row")
         traffic = int(per_row * sum(p + 1 for p in pos)) if per_row else None
+    per_step_launches = L.qwen_b200_batch_launches_per_step(batch)
     L.qwen_b200_batch_free(batch)
     parity = None
     if getattr(args, "ref_check", False) and world == 1:
@@ -539,7 +540,7 @@ def run_batched(args, cfg, world, rank, local, dist, torch):
                    "l2": "inputs larger than L2 (weights and K/V stream from HBM every step)"},
         "e2e": {"value": round(e2e_steps * tokens_total / steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * 16},
-        "gpu_launches": (shape.layers * 8 + 4) * (steps + max(args.warmup, 3)),
+        "gpu_launches": per_step_launches * (steps + max(args.warmup, 3)),
         "roofline": {"bound": "hbm",
                      "kernel": "batch_attn_tc_kernel + batch_attn_merge_kernel (64 sessions x 2 KV heads, "
                                "split-K flash decoding on TF32 tensor-core fragments)",

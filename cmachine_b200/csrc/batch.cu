@@ -67,8 +67,12 @@ struct RmsArgs {
     const uint16_t *embed;    // layer 0: x <- E[token] first
     float eps;
     int copy_x;               // final norm: also copy x to the session's buffer
+    const float *part;        // or the residual GEMM's deferred K-split partials: x += their sum first
 };
-__global__ void __launch_bounds__(256) batch_rms_kernel(RmsArgs a) {
+// K splits of a residual GEMM (O, down) whose partials the next RMSNorm sums:
+// 12 tiles x 12 splits = 144 CTAs, one wave on 148 SMs.
+constexpr int kResidSplits = 12;
+__global__ void __launch_bounds__(256, 1) batch_rms_kernel(RmsArgs a) {
     __shared__ float red[8];
     pdl_trigger();
     pdl_wait();
@@ -86,6 +90,29 @@ __global__ void __launch_bounds__(256) batch_rms_kernel(RmsArgs a) {
     } else {
 #pragma unroll
         for (int i = 0; i < kHd / 256; i++) v[i] = x[tid + 256 * i];
+    }
+    if (a.part) {
+        // x += the residual GEMM's output, as its K-split partials summed in
+        // split order (partial layout [tile][split][session][128]); all 72
+        // loads are issued before the sums.
+        float p[kHd / 256][kResidSplits];
+#pragma unroll
+        for (int i = 0; i < kHd / 256; i++) {
+            const int j = tid + 256 * i;
+            const float *src = a.part + ((size_t)(j >> 7) * kResidSplits * kBN + n) * 128 + (j & 127);
+#pragma unroll
+            for (int sp = 0; sp < kResidSplits; sp++)  // volatile: kept ahead of every sum below
+                asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(p[i][sp]) : "l"(src + (size_t)sp * kBN * 128));
+        }
+#pragma unroll
+        for (int i = 0; i < kHd / 256; i++) {
+            float sum = 0.f;
+#pragma unroll
+            for (int sp = 0; sp < kResidSplits; sp++)  // volatile: not hoisted between the loads
+                asm volatile("add.rn.f32 %0, %0, %1;" : "+f"(sum) : "f"(p[i][sp]));
+            v[i] = __fadd_rn(v[i], sum);
+            x[tid + 256 * i] = v[i];
+        }
     }
     float ss = 0.f;
 #pragma unroll
@@ -173,6 +200,7 @@ __device__ __forceinline__ int pair_row(int i, int p0, int np) {
     const int k = i % (2 * np);
     return k < np ? p0 + k : 64 + p0 + (k - np);
 }
+
 // x += D (the O and down projections): tile rows are output rows t*128 ...
 // The loads of a group of items are issued together, then the sums stored.
 struct EpiResid {
@@ -1116,11 +1144,11 @@ struct QwenB200Batch {
     int cluster_qkv, cluster_o, cluster_down;  // split clusters (0: split K through global memory)
     int attn_item_rows;   // cache rows per attention work item
     int attn_kernel;      // 0: tensor-core fragments + merge kernel; 1: CUDA-core flash-decoding
+    int resid_defer;      // 1: the O and down GEMMs leave K-split partials that the next RMSNorm sums
     TcmTop2 *log, *host_log;
     unsigned long long *trace;  // stage timeline (measurement only), or null
     int readout_tiles;
     std::map<int, cudaGraphExec_t> graphs;
-    int launches;
     float *prefill_logits, *prefill_x;  // logits and hidden rows of a prefill chunk's non-final tokens (lazy)
 };
 
@@ -1129,7 +1157,7 @@ namespace {
 template <class Epi>
 void launch_gemm(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1, const CUtensorMap &a2,
                  const CUtensorMap &xh, const CUtensorMap &xl, int tiles, int splits, int kblocks, const Epi &epi,
-                 bool pdl, int cluster = 1) {
+                 bool pdl, int cluster = 1, bool defer = false) {
     TcArgs<kBN, Epi> args;
     args.a[0] = a0;
     args.a[1] = a1;
@@ -1140,6 +1168,7 @@ void launch_gemm(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1,
     args.splits = splits;
     args.kblocks = kblocks;
     args.cluster = cluster;
+    args.defer = defer ? 1 : 0;
     args.part = b->part;
     args.counters = b->counters;
     args.err = &b->st->err;
@@ -1170,12 +1199,14 @@ void launch_gemm(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1,
 }
 
 // A K-split GEMM of `tiles` 128-row tiles: split across a cluster when one
-// fits (cluster > 0), else 12 splits meeting in global memory.
+// fits (cluster > 0), else 12 splits meeting in global memory; with
+// defer_splits > 0, that many splits whose partials the next kernel sums.
 template <class Epi>
 void launch_split(QwenB200Batch *b, const CUtensorMap &a0, const CUtensorMap &a1, const CUtensorMap &a2,
                   const CUtensorMap &xh, const CUtensorMap &xl, int tiles, int kblocks, const Epi &epi, bool pdl,
-                  int cluster) {
-    if (cluster > 0) launch_gemm(b, a0, a1, a2, xh, xl, tiles, cluster, kblocks, epi, pdl, cluster);
+                  int cluster, int defer_splits = 0) {
+    if (defer_splits > 0) launch_gemm(b, a0, a1, a2, xh, xl, tiles, defer_splits, kblocks, epi, pdl, 1, true);
+    else if (cluster > 0) launch_gemm(b, a0, a1, a2, xh, xl, tiles, cluster, kblocks, epi, pdl, cluster);
     else launch_gemm(b, a0, a1, a2, xh, xl, tiles, kblocks < 12 ? kblocks : 12, kblocks, epi, pdl, 1);
 }
 
@@ -1207,10 +1238,20 @@ int pick_cluster(int tiles, int kblocks) {
     return 0;
 }
 
-void launch_rms(QwenB200Batch *b, const float *w, bool embed, bool copy_x, bool pdl) {
+// fold: the residual GEMM before this launch deferred its K-split sum here.
+void launch_rms(QwenB200Batch *b, const float *w, bool embed, bool copy_x, bool pdl, bool fold = false) {
     RmsArgs a = {b->st, b->x, w, b->nh, b->nl, embed ? (const uint16_t *)b->embed_ptr : nullptr, b->s.epsilon,
-                 copy_x ? 1 : 0};
+                 copy_x ? 1 : 0, fold ? b->part : nullptr};
     launch(batch_rms_kernel, dim3(kBN), dim3(256), 0, stream(), pdl, a);
+}
+
+// The q/k/v projection of `layer` (bias, RoPE and K/V append in its epilogue,
+// so its K splits meet in a cluster fold inside the GEMM).
+void launch_qkv(QwenB200Batch *b, int layer, bool pdl) {
+    const std::vector<QwenB200Layer> &L = *b->layers;
+    const LayerMaps &m = b->maps[layer];
+    EpiQkv qkv = {b->st, L[layer].qb, L[layer].kb, L[layer].vb, b->rope_den, b->q, layer};
+    launch_split(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, kHd / kTcKBlock, qkv, pdl, b->cluster_qkv);
 }
 
 // The attention of `layer` for n sessions (and its merge, for the tensor-core kernel).
@@ -1232,19 +1273,21 @@ void launch_step(QwenB200Batch *b, int n) {
     launch_rms(b, L[0].input_norm, true, false, false);
     for (int l = 0; l < s.layers; l++) {
         const LayerMaps &m = b->maps[l];
-        EpiQkv qkv = {b->st, L[l].qb, L[l].kb, L[l].vb, b->rope_den, b->q, l};
-        launch_split(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, kHd / kTcKBlock, qkv, true, b->cluster_qkv);
+        launch_qkv(b, l, true);
         launch_attention(b, l, n, nullptr, true);
+        const bool defer = b->resid_defer != 0;
         EpiResid o = {b->st, b->x};
-        launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, true, b->cluster_o);
-        launch_rms(b, L[l].post_norm, false, false, true);
+        launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, true, b->cluster_o,
+                     defer ? kResidSplits : 0);
+        launch_rms(b, L[l].post_norm, false, false, true, defer);
         EpiSwiglu sw = {b->st, b->hh, b->hl};
         launch_gemm(b, m.gate, m.up, m.up, b->nh_map, b->nl_map, kFf / 64, 1, kHd / kTcKBlock, sw, true);
         EpiResid dn = {b->st, b->x};
-        launch_split(b, m.down, m.down, m.down, b->hh_map, b->hl_map, 12, kFf / kTcKBlock, dn, true, b->cluster_down);
-        if (l + 1 < s.layers) launch_rms(b, L[l + 1].input_norm, false, false, true);
+        launch_split(b, m.down, m.down, m.down, b->hh_map, b->hl_map, 12, kFf / kTcKBlock, dn, true, b->cluster_down,
+                     defer ? kResidSplits : 0);
+        if (l + 1 < s.layers) launch_rms(b, L[l + 1].input_norm, false, false, true, defer);
     }
-    launch_rms(b, b->final_norm, false, true, true);
+    launch_rms(b, b->final_norm, false, true, true, b->resid_defer != 0);
     EpiLogits lg = {b->st};
     launch_gemm(b, b->embed, b->embed, b->embed, b->nh_map, b->nl_map, b->readout_tiles, 1, kHd / kTcKBlock, lg, true);
     Top2Args ta = {b->st, b->top_part, b->top_counters, b->s.vocab, b->log};
@@ -1378,6 +1421,7 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
     b->hh_map = bf16_map(b->hh, kFf, kBN, kBN);
     b->hl_map = bf16_map(b->hl, kFf, kBN, kBN);
     b->part = (float *)gpu_alloc((size_t)16 * 12 * 128 * kBN * 4);
+    gpu_zero(b->part, (size_t)16 * 12 * 128 * kBN * 4);  // a stage timed alone may read partials no GEMM wrote
     b->counters = (unsigned *)gpu_alloc(256 * 4);
     gpu_zero(b->counters, 256 * 4);
     b->attn_part = (float *)gpu_alloc((size_t)kBN * 2 * kAttnItemMax * kAttnPartialFloats * 4);
@@ -1392,12 +1436,12 @@ QwenB200Batch *qwen_b200_batch_create(const QwenB200Decoder *d) {
     gpu_zero(b->attn_work, (size_t)s.layers * 2 * 4);
     b->attn_item_rows = kTcItemRowsDefault;
     b->attn_kernel = 0;
+    b->resid_defer = 1;
     b->cluster_qkv = pick_cluster(16, kHd / kTcKBlock);
     b->cluster_o = pick_cluster(12, kHd / kTcKBlock);
     b->cluster_down = pick_cluster(12, kFf / kTcKBlock);
     b->log = (TcmTop2 *)gpu_alloc(sizeof(TcmTop2) * kBatchLogCap * kBN);
     TCM_CUDA(cudaMallocHost((void **)&b->host_log, sizeof(TcmTop2) * kBatchLogCap * kBN));
-    b->launches = 1 + s.layers * 7 + 3;
     return b;
 }
 
@@ -1420,16 +1464,18 @@ int qwen_b200_batch_max(void) { return kBN; }
 int qwen_b200_batch_tune(QwenB200Batch *b, int key, int value) {
     if (!b) return -1;
     if (key == 0 && (value < kAttnItemRowsMin || value > 2048 || value % kAttnRowsPerStage)) return -1;
-    if (key == 1 && value != 0 && value != 1) return -1;
-    if (key != 0 && key != 1) return -1;
+    if ((key == 1 || key == 2) && value != 0 && value != 1) return -1;
+    if (key < 0 || key > 2) return -1;
     TCM_CUDA(cudaStreamSynchronize(stream()));
     for (auto &g : b->graphs) TCM_CUDA(cudaGraphExecDestroy(g.second));
     b->graphs.clear();
     if (key == 0) {  // attention rows per work item
         b->attn_item_rows = value;
-    } else {  // attention kernel, with its own default item size
+    } else if (key == 1) {  // attention kernel, with its own default item size
         b->attn_kernel = value;
         b->attn_item_rows = value == 0 ? kTcItemRowsDefault : 1024;
+    } else {  // O and down: K-split sum in the next RMSNorm (1) or in a cluster fold (0)
+        b->resid_defer = value;
     }
     return 0;
 }
@@ -1469,8 +1515,7 @@ float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSes
     auto once = [&]() {
         switch (stage) {
             case 0: {
-                EpiQkv qkv = {b->st, L[layer].qb, L[layer].kb, L[layer].vb, b->rope_den, b->q, layer};
-                launch_split(b, m.q, m.k, m.v, b->nh_map, b->nl_map, 16, kHd / kTcKBlock, qkv, false, b->cluster_qkv);
+                launch_qkv(b, layer, false);
                 break;
             }
             case 1: {
@@ -1479,7 +1524,8 @@ float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSes
             }
             case 2: {
                 EpiResid o = {b->st, b->x};
-                launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, false, b->cluster_o);
+                launch_split(b, m.o, m.o, m.o, b->nh_map, b->nl_map, 12, kHd / kTcKBlock, o, false, b->cluster_o,
+                             b->resid_defer ? kResidSplits : 0);
                 break;
             }
             case 3: {
@@ -1490,7 +1536,7 @@ float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSes
             case 4: {
                 EpiResid dn = {b->st, b->x};
                 launch_split(b, m.down, m.down, m.down, b->hh_map, b->hl_map, 12, kFf / kTcKBlock, dn, false,
-                             b->cluster_down);
+                             b->cluster_down, b->resid_defer ? kResidSplits : 0);
                 break;
             }
             case 5: {
@@ -1499,7 +1545,7 @@ float qwen_b200_batch_time_stage(QwenB200Batch *b, int n, const QwenB200BatchSes
                             kHd / kTcKBlock, lg, false);
                 break;
             }
-            default: launch_rms(b, L[layer].post_norm, false, false, false); break;
+            default: launch_rms(b, L[layer].post_norm, false, false, false, b->resid_defer != 0); break;
         }
     };
     once();
@@ -1541,6 +1587,7 @@ int qwen_b200_batch_matmul(const void *w, int rows, int in, const float *x, int 
     a.splits = splits;
     a.kblocks = in / 64;
     a.cluster = 1;
+    a.defer = 0;
     a.part = part;
     a.counters = counters;
     a.err = err;
@@ -1557,7 +1604,12 @@ int qwen_b200_batch_matmul(const void *w, int rows, int in, const float *x, int 
     }
     return 0;
 }
-int qwen_b200_batch_launches_per_step(const QwenB200Batch *b) { return b ? b->launches : 0; }
+int qwen_b200_batch_launches_per_step(const QwenB200Batch *b) {
+    // First RMSNorm; per layer q/k/v, attention (+ its merge), O, RMSNorm,
+    // gate/up, down, and the next RMSNorm (the final one after the last
+    // layer); vocabulary GEMM, top-2, step end.
+    return b ? 1 + b->s.layers * (7 + (b->attn_kernel == 0 ? 1 : 0)) + 3 : 0;
+}
 
 int qwen_b200_batch_step(QwenB200Batch *b, int n, const QwenB200BatchSession *sessions, const int *tokens,
                          const int *positions, TcmTop2 *tops) {

@@ -22,7 +22,9 @@
 //           32 * (w % 4) ..., warps 2-5 the first half of the columns and
 //           warps 6-9 the second), then either the tile's final values or, with
 //           split K, a partial to global memory of which the last CTA to arrive
-//           sums the splits in order (deterministic) and finishes the tile.
+//           sums the splits in order (deterministic) and finishes the tile, or
+//           (defer) a partial that the next kernel sums while it reads the
+//           tile's outputs anyway.
 //           The epilogue's per-element work (folds, bias, RoPE, SwiGLU, BF16
 //           splits) is latency-bound, so two warps per scheduler run it.
 // With split K launched as thread-block clusters (one cluster of `splits` CTAs
@@ -125,6 +127,8 @@ template <int N, class Epi> struct TcArgs {
     CUtensorMap xh, xl;
     int tiles, splits, kblocks;
     int cluster;          // 1: splits meet in global memory; = splits: in a thread-block cluster
+    int defer = 0;        // 1 (with cluster 1): every split leaves its partial in `part` as
+                          // [tile][split][session][128] and the next kernel sums them (no fold here)
     float *part;          // split-K partials [tile][split][128][N]
     unsigned *counters;   // per tile, reset by the finishing CTA
     unsigned *err;
@@ -303,6 +307,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 epi_sync();
 #pragma unroll
                 for (int c = 0; c < H; c++) tile[rr][c0 + c] = v[c];
+                continue;
+            }
+            if (a.defer) {
+                // Deferred fold: the partial goes out in the layout its reader
+                // wants, each session's 128 rows contiguous (a warp's 32 lanes
+                // are 32 consecutive rows, so every store is one 128-byte line).
+                float *p = a.part + ((size_t)t * a.splits + item % a.splits) * N * 128 + rr;
+#pragma unroll
+                for (int c = 0; c < H; c++) p[(size_t)(c0 + c) * 128] = v[c];
                 continue;
             }
             bool finish = true;

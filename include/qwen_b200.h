@@ -200,8 +200,10 @@ int qwen_b200_batch_cluster_capacity(int size);
 /* Tuning: key 0 = cache rows per attention work item (a multiple of 32 in
  * [256, 2048]); key 1 = the attention kernel: 0 tensor-core fragments (the
  * default, items of 256 rows), 1 CUDA-core flash-decoding (items of 1024
- * rows); choosing a kernel resets the item size to its default. Returns 0, or
- * -1 for an unknown key or value. */
+ * rows); choosing a kernel resets the item size to its default; key 2 = where
+ * the O and down projections' K splits are summed: 1 in the RMSNorm that reads
+ * their output next (the default), 0 in a thread-block cluster fold inside the
+ * GEMM. Returns 0, or -1 for an unknown key or value. */
 int qwen_b200_batch_tune(QwenB200Batch *, int key, int value);
 int qwen_b200_batch_clusters(const QwenB200Batch *, int *qkv, int *o, int *down);
 
