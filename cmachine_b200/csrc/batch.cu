@@ -72,67 +72,73 @@ struct RmsArgs {
 // K splits of a residual GEMM (O, down) whose partials the next RMSNorm sums:
 // 12 tiles x 12 splits = 144 CTAs, one wave on 148 SMs.
 constexpr int kResidSplits = 12;
-__global__ void __launch_bounds__(256, 1) batch_rms_kernel(RmsArgs a) {
-    __shared__ float red[8];
+constexpr int kRmsThreads = kHd / 4;  // 384: four consecutive elements of x a thread
+__global__ void __launch_bounds__(kRmsThreads, 1) batch_rms_kernel(RmsArgs a) {
+    __shared__ float red[kRmsThreads / 32];
+    const int n = blockIdx.x, tid = threadIdx.x, j0 = 4 * tid;
+    float w[4];  // norm weights: constants, read before the dependency wait
+#pragma unroll
+    for (int c = 0; c < 4; c++) w[c] = a.w[j0 + c];
     pdl_trigger();
     pdl_wait();
-    const int n = blockIdx.x, tid = threadIdx.x;
     if (n >= a.st->n) return;
-    float v[kHd / 256];
-    float *x = a.x + (size_t)n * kHd;
+    float v[4];
+    float *x = a.x + (size_t)n * kHd + j0;
     if (a.embed) {
-        const uint16_t *row = a.embed + (size_t)a.st->token[n] * kHd;
-#pragma unroll
-        for (int i = 0; i < kHd / 256; i++) {
-            v[i] = __uint_as_float((uint32_t)row[tid + 256 * i] << 16);
-            x[tid + 256 * i] = v[i];
-        }
+        const uint2 e = *reinterpret_cast<const uint2 *>(a.embed + (size_t)a.st->token[n] * kHd + j0);  // 4 BF16
+        v[0] = __uint_as_float(e.x << 16);
+        v[1] = __uint_as_float(e.x & 0xffff0000u);
+        v[2] = __uint_as_float(e.y << 16);
+        v[3] = __uint_as_float(e.y & 0xffff0000u);
+        *reinterpret_cast<float4 *>(x) = make_float4(v[0], v[1], v[2], v[3]);
     } else {
-#pragma unroll
-        for (int i = 0; i < kHd / 256; i++) v[i] = x[tid + 256 * i];
+        const float4 t = *reinterpret_cast<const float4 *>(x);
+        v[0] = t.x;
+        v[1] = t.y;
+        v[2] = t.z;
+        v[3] = t.w;
     }
     if (a.part) {
         // x += the residual GEMM's output, as its K-split partials summed in
-        // split order (partial layout [tile][split][session][128]); all 72
-        // loads are issued before the sums.
-        float p[kHd / 256][kResidSplits];
+        // split order (partial layout [tile][split][session][128]); the 12
+        // 16-byte loads are issued before the sums.
+        const float *src = a.part + ((size_t)(j0 >> 7) * kResidSplits * kBN + n) * 128 + (j0 & 127);
+        float p[kResidSplits][4];
 #pragma unroll
-        for (int i = 0; i < kHd / 256; i++) {
-            const int j = tid + 256 * i;
-            const float *src = a.part + ((size_t)(j >> 7) * kResidSplits * kBN + n) * 128 + (j & 127);
+        for (int sp = 0; sp < kResidSplits; sp++)  // volatile: kept ahead of every sum below
+            asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(p[sp][0]), "=f"(p[sp][1]), "=f"(p[sp][2]), "=f"(p[sp][3])
+                         : "l"(src + (size_t)sp * kBN * 128));
 #pragma unroll
-            for (int sp = 0; sp < kResidSplits; sp++)  // volatile: kept ahead of every sum below
-                asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(p[i][sp]) : "l"(src + (size_t)sp * kBN * 128));
-        }
-#pragma unroll
-        for (int i = 0; i < kHd / 256; i++) {
+        for (int c = 0; c < 4; c++) {
             float sum = 0.f;
 #pragma unroll
             for (int sp = 0; sp < kResidSplits; sp++)  // volatile: not hoisted between the loads
-                asm volatile("add.rn.f32 %0, %0, %1;" : "+f"(sum) : "f"(p[i][sp]));
-            v[i] = __fadd_rn(v[i], sum);
-            x[tid + 256 * i] = v[i];
+                asm volatile("add.rn.f32 %0, %0, %1;" : "+f"(sum) : "f"(p[sp][c]));
+            v[c] = __fadd_rn(v[c], sum);
         }
+        *reinterpret_cast<float4 *>(x) = make_float4(v[0], v[1], v[2], v[3]);
     }
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < kHd / 256; i++) ss = fmaf(v[i], v[i], ss);
+    for (int c = 0; c < 4; c++) ss = fmaf(v[c], v[c], ss);
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
     float total = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; w++) total += red[w];
+    for (int k = 0; k < kRmsThreads / 32; k++) total += red[k];
     const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)kHd), a.eps)));
+    uint16_t h[4], l[4];
 #pragma unroll
-    for (int i = 0; i < kHd / 256; i++) {
-        const int j = tid + 256 * i;
-        uint16_t h, l;
-        split_bf16(__fmul_rn(__fmul_rn(v[i], r), a.w[j]), h, l);
-        a.hi[(size_t)n * kHd + j] = h;
-        a.lo[(size_t)n * kHd + j] = l;
-        if (a.copy_x) a.st->x[n][j] = v[i];
-    }
+    for (int c = 0; c < 4; c++) split_bf16(__fmul_rn(__fmul_rn(v[c], r), w[c]), h[c], l[c]);
+    *reinterpret_cast<uint2 *>(a.hi + (size_t)n * kHd + j0) =
+        make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+    *reinterpret_cast<uint2 *>(a.lo + (size_t)n * kHd + j0) =
+        make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
+    if (a.copy_x)  // the caller's buffer: no alignment assumed
+#pragma unroll
+        for (int c = 0; c < 4; c++) a.st->x[n][j0 + c] = v[c];
 }
 
 // ---------------------------------------------------------------- GEMM epilogues
@@ -1242,7 +1248,7 @@ int pick_cluster(int tiles, int kblocks) {
 void launch_rms(QwenB200Batch *b, const float *w, bool embed, bool copy_x, bool pdl, bool fold = false) {
     RmsArgs a = {b->st, b->x, w, b->nh, b->nl, embed ? (const uint16_t *)b->embed_ptr : nullptr, b->s.epsilon,
                  copy_x ? 1 : 0, fold ? b->part : nullptr};
-    launch(batch_rms_kernel, dim3(kBN), dim3(256), 0, stream(), pdl, a);
+    launch(batch_rms_kernel, dim3(kBN), dim3(kRmsThreads), 0, stream(), pdl, a);
 }
 
 // The q/k/v projection of `layer` (bias, RoPE and K/V append in its epilogue,
