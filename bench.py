@@ -203,11 +203,33 @@ def prompt_tokens(seed: int, n: int, vocab: int):
 
 
 # ---------------------------------------------------------------- CPU baseline (reference path)
-def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: int | None = None):
+def ref_context(cfg) -> int:
+    """Cached rows the CPU reference starts from for a configuration: the prompt
+    length of a batch-1 workload, the mean context of the batched one."""
+    if "prompt" in cfg:
+        return cfg["prompt"]
+    if "ctx" in cfg:
+        return (cfg["ctx"][0] + cfg["ctx"][1]) // 2
+    return 0
+
+
+def context_kv(layers: int, context: int):
+    """Seeded K/V rows standing for a `context`-token prompt, shared by the CPU
+    sample's sessions and its GPU replay: kv[layer][kind] = [kvheads][context][128]."""
+    import numpy as np
+    rng = np.random.default_rng(5150 + context)
+    return [[(0.5 * rng.standard_normal((2, context, 128))).astype(np.float32) for _ in (0, 1)]
+            for _ in range(layers)]
+
+
+def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: int | None = None, context: int = 0):
     """The reference's own CPU FP32 C path (src/qwen.c + tests/gpu_stub.c, built
-    from its sources into oracle/_ref), one session per host thread, each
-    decoding from a 2-token prompt; returns (tokens/s, threads, sample, kind,
-    the first thread's logits per step)."""
+    from its sources into oracle/_ref), one session per host thread. With
+    `context`, every session starts after `context` cached rows (seeded K/V rows
+    written into the reference session, cursor placed after them), so each
+    token's attention reads the workload's cache length; then one prompt token
+    and greedy steps. Returns (tokens/s, threads, sample, kind, the first
+    thread's logits per greedy step)."""
     sys.path.insert(0, str(ROOT / "tests"))
     import ctypes
     import numpy as np
@@ -215,15 +237,21 @@ def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: 
     L, model, kind = reference_model(layers, 2 if bf16 else 0, 2026)
     shape = cm.qwen_shape(layers, 32768)
     n = threads or max(1, min(os.cpu_count() or 1, 32))
-    per_token = 1.3 * layers / 28 + 0.05
+    per_token = (1.3 * layers / 28 + 0.05) * (1.0 + context / 16000.0)
     steps = max(2, int(seconds / max(per_token, 1e-3)) // 1)
     steps = min(steps, 12 if layers > 2 else 64)
     results, first_logits = [0] * n, []
+    kv = context_kv(layers, context) if context else None
 
     def worker(i):
-        s = L.orc_session_create(model, 64)
+        s = L.orc_session_create(model, context + 64)
+        if kv:
+            for layer in range(layers):
+                for kind in (0, 1):
+                    L.orc_write_kv(s, layer, kind, context, ctypes.c_void_p(kv[layer][kind].ctypes.data))
+            assert L.orc_set_cursor(s, context) == 0
         top = cm.Top2()
-        toks = prompt_tokens(90 + i, 2, shape.vocab)
+        toks = prompt_tokens(90 + i, 1 if kv else 2, shape.vocab)
         out = np.empty(shape.vocab, np.float32)
         for t in toks:
             L.orc_push(s, t, ctypes.byref(top), ctypes.c_void_p(out.ctypes.data))
@@ -244,7 +272,8 @@ def cpu_reference_rate(layers: int, bf16: bool, seconds: float = 15.0, threads: 
         th.join()
     wall = time.perf_counter() - t0
     total = sum(results)
-    sample = (f"{n} threads x (2-token prompt + {steps} greedy decode steps, every push counted), {layers}-layer "
+    start = f"{context} cached rows (seeded K/V) + 1 prompt token" if context else "2-token prompt"
+    sample = (f"{n} threads x ({start} + {steps} greedy decode steps, every push counted), {layers}-layer "
               f"{'BF16' if bf16 else 'FP32'} seeded model, one session per thread")
     return total / wall, n, sample, kind, first_logits
 
@@ -617,16 +646,24 @@ def session_kv(session, layers: int):
     return [[session.kv(layer, kind) for kind in (0, 1)] for layer in range(layers)]
 
 
-def gpu_dlogit(layers: int, profile: int, ref_logits):
-    """max |delta logit| of the GPU path on the CPU sample's first thread."""
+def gpu_dlogit(layers: int, profile: int, ref_logits, context: int = 0):
+    """max |delta logit| of the GPU path on the CPU sample's first thread (the
+    same context rows, prompt and greedy steps)."""
     import numpy as np
     import cmachine_b200 as cm
     if not ref_logits:
         return None
-    model = cm.Model(cm.qwen_shape(layers, 4096), 2026, cm.BENCH_LAW, profile)
-    s = cm.Session(model, 64)
+    model = cm.Model(cm.qwen_shape(layers, 32768), 2026, cm.BENCH_LAW, profile)
+    s = cm.Session(model, context + 64)
     worst = 0.0
-    for t in prompt_tokens(90, 2, model.shape.vocab):
+    toks = prompt_tokens(90, 1 if context else 2, model.shape.vocab)
+    if context:
+        kv = context_kv(layers, context)
+        for layer in range(layers):
+            for kind in (0, 1):
+                s.write_kv(layer, kind, kv[layer][kind])
+        assert s.set_cursor(context, toks[0]) == 0
+    for t in toks:
         s.push(t)
     for ref in ref_logits:
         s.push(s.pending)
@@ -637,6 +674,16 @@ def gpu_dlogit(layers: int, profile: int, ref_logits):
 
 
 # ---------------------------------------------------------------- B200 arm
+def batch1_config(name: str, cfg, world: int, tp: bool = False):
+    """The workload of a batch-1 configuration, as both arms report it."""
+    return {"workload": f"qwen2.5-1.5b-{name}", "layers": cfg["layers"], "batch": 1,
+            "prompt_tokens": cfg["prompt"], "decode_window": cfg["window"],
+            "weights": "seeded N(0,0.02) random init",
+            "parallelism": f"tensor{world} (MLP units and readout rows split, peer-memory exchange)" if tp
+            else f"replicas{world}",
+            "l2": "inputs larger than L2 (weights stream from HBM every step)"}
+
+
 def run_b200(args, cfg, world, rank, local, dist, torch, tp=False):
     """Batch-1 decode: one independent session per GPU, or with tp one session
     split over all the GPUs (tensor-parallel MLP and readout)."""
@@ -756,12 +803,8 @@ def run_b200(args, cfg, world, rank, local, dist, torch, tp=False):
         "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
         "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "strong" if tp else "weak",
         "vs_baseline": None, "dtype": "bf16-weights/f32" if es == 2 else "f32", "data": "synthetic",
-        "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": shape.layers, "batch": 1,
-                   "prompt_tokens": cfg["prompt"], "decode_window": window, "token_execution": args.token_mode,
-                   "weights": "seeded N(0,0.02) random init",
-                   "parallelism": f"tensor{world} (MLP units and readout rows split, peer-memory exchange)" if tp
-                   else f"replicas{world}",
-                   "l2": "inputs larger than L2 (weights stream from HBM every step)"},
+        "config": batch1_config(args.config, cfg, world, tp),
+        "execution": {"token": args.token_mode},
         "e2e": {"value": round(args.steps * sessions / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 32},
         "gpu_launches": per_token_launches * args.steps + (args.steps + window - 1) // window,
@@ -810,13 +853,15 @@ def main():
                 return
             rate, cores, sample, kind = got
         else:
-            rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
+            rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2,
+                                                              context=ref_context(cfg))
         print(json.dumps({
             "metric": METRIC, "impl": "reference", "value": round(rate, 4), "unit": "tokens/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16-weights/f32" if cfg["profile"] == 2 else "f32", "data": "synthetic",
-            "config": {"workload": f"qwen2.5-1.5b-{args.config}", "layers": cfg["layers"], "batch": 1},
+            "config": (batch1_config(args.config, cfg, int(os.environ.get("WORLD_SIZE", "1"))) if "prompt" in cfg
+                       else {"workload": f"qwen2.5-1.5b-{args.config}", "layers": cfg["layers"], "batch": 1}),
             "cpu_baseline": {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                              "sample": sample},
             "e2e": {"value": round(rate, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -876,7 +921,7 @@ def run_workload(args, name, world, rank, local, dist, torch, cpu=False):
     if "batch" in cfg:
         line = run_batched(sub, cfg, world, rank, local, dist, torch)
         if cpu and rank == 0 and world == 1:
-            rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], True)
+            rate, cores, sample, kind, _ = cpu_reference_rate(cfg["layers"], True, context=ref_context(cfg))
             line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                                     "sample": sample + "; at these sessions' contexts the reference's attention adds "
                                               "about a quarter to each token's arithmetic"}
@@ -892,10 +937,11 @@ def run_workload(args, name, world, rank, local, dist, torch, cpu=False):
         return line
     line = run_b200(sub, cfg, world, rank, local, dist, torch)
     if cpu and rank == 0 and world == 1:
-        rate, cores, sample, kind, ref_logits = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2)
+        rate, cores, sample, kind, ref_logits = cpu_reference_rate(cfg["layers"], cfg["profile"] == 2,
+                                                                   context=ref_context(cfg))
         line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                                 "sample": sample}
-        line["max_abs_dlogit"] = gpu_dlogit(cfg["layers"], cfg["profile"], ref_logits)
+        line["max_abs_dlogit"] = gpu_dlogit(cfg["layers"], cfg["profile"], ref_logits, context=ref_context(cfg))
     return line
 
 
