@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
     constexpr int R = Geo<WT>::R;
     __shared__ __align__(16) float in_s[kHidden];
     __shared__ float ml_s[kFoldHeads][kClustersPerHead][2 * kAttnMaxGroup];
+    __shared__ float x_s[kMaxRowsPerCta];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = share_begin(kHidden, blockIdx.x, gridDim.x), r1 = share_begin(kHidden, blockIdx.x + 1, gridDim.x);
     const int items = r1 - r0;
@@ -245,6 +246,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
     }
     pdl_wait();
     trace_mark(a.trace, 1);
+    // This CTA's residual rows, read now so that no row's update waits on L2
+    // after its dot product (published by the consumers_sync below).
+    if ((int)threadIdx.x < items) x_s[threadIdx.x] = a.x[r0 + threadIdx.x];
     if (a.part) fold_attention(in_s, ml_s, a.part, a.group);
     else copy_hidden(in_s, a.in);
     consumers_sync();
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) oproj_kernel(ORowsArgs a) {
             const int j = warp + kConsumerWarps * m;
             if (j < n) {
                 const float y = row_dot<WT>(stage + (size_t)j * kRow<WT>, xr, lane);
-                if (lane == 0) a.x[r0 + g * R + j] = __fadd_rn(a.x[r0 + g * R + j], y);
+                if (lane == 0) a.x[r0 + g * R + j] = __fadd_rn(x_s[g * R + j], y);
             }
         }
         ring_release(ring, g);
@@ -378,6 +382,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
     using G = DownGeo<WT, SH>;
     constexpr int RD = G::RD, E = G::E, PIECES = G::PIECES, RPW = G::RPW, NVP = G::NVP, KV = G::KV;
     __shared__ float part_s[2][RD][PIECES];
+    __shared__ float x_s[kMaxRowsPerCta];
     __shared__ int fail_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int piece = PIECES > 1 ? warp % PIECES : 0;
@@ -396,6 +401,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
     }
     pdl_wait();
     trace_mark(a.trace, 1);
+    // This CTA's residual rows, read now (published by the first consumers_sync).
+    if ((int)threadIdx.x < items) x_s[threadIdx.x] = a.x[r0 + threadIdx.x];
     float hr[KV * E];
 #pragma unroll
     for (int k = 0; k < KV; k++) {
@@ -445,7 +452,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
                 const size_t at = ((size_t)a.layer * a.tp.world + a.tp.rank) * kHidden + row;
                 for (int p = 0; p < a.tp.world; p++) ll_store(a.tp.part[p] + at, __float_as_uint(sum), token);
             } else {
-                a.x[row] = __fadd_rn(a.x[row], sum);
+                a.x[row] = __fadd_rn(x_s[g * RD + s], sum);
             }
         }
     }
@@ -461,7 +468,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) down_kernel(DownArgs a) {
                 ok = ll_wait(mine + (size_t)p * kHidden + row, token, &bits, &a.st->fault);
                 sum = p ? __fadd_rn(sum, __uint_as_float(bits)) : __uint_as_float(bits);
             }
-            if (ok) a.x[row] = __fadd_rn(a.x[row], sum);
+            if (ok) a.x[row] = __fadd_rn(x_s[row - r0], sum);
         }
     }
     trace_mark(a.trace, 3);
@@ -1174,6 +1181,9 @@ QwenB200Runner *qwen_b200_runner_create(const QwenB200Decoder *d, const QwenB200
     r->attn_counters = (unsigned *)gpu_alloc((size_t)d->s.kvheads * sizeof(unsigned));
     gpu_zero(r->attn_counters, (size_t)d->s.kvheads * sizeof(unsigned));
     r->grid = sm_count();
+    if (r->grid * kMaxRowsPerCta < kHidden)  // the O and down kernels stage their residual rows per CTA
+        TCM_FATAL("qwen_b200: %d SMs is too few for the fused decoder (needs %d)", r->grid,
+                  (kHidden + kMaxRowsPerCta - 1) / kMaxRowsPerCta);
     r->top_pv = (float *)gpu_alloc((size_t)4 * r->grid * sizeof(float));  // two per CTA, up to two CTAs per SM
     r->top_pi = (int *)gpu_alloc((size_t)4 * r->grid * sizeof(int));
     r->sync = (unsigned *)gpu_alloc(2 * sizeof(unsigned));

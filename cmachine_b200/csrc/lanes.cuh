@@ -29,6 +29,7 @@ constexpr int kRingRowBytes = 528;  // one ring row: 4 x 128 codes + 4 FP32 scal
 constexpr int kHidden = 1536;       // Qwen2.5-1.5B hidden size (the fused kernels' geometry)
 constexpr int kInter = 8960;        // MLP width
 constexpr int kMaxPairsPerCta = 64; // q/k/v row pairs one CTA may own
+constexpr int kMaxRowsPerCta = 64;  // residual rows one O or down CTA may own (grids of at least 24 CTAs)
 
 // Weight geometry: E elements per 16-byte vector; R rows of 1536 per stage
 // (48 KB either way); RD rows of 8960 per down stage (35 KB).
