@@ -50,6 +50,18 @@ def test_reference_arm_line():
     assert line["impl"] == "reference" and line["unit"] == "tokens/s" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference"
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+    # The reference arm reports the B200 arm's workload object, and its sample
+    # decodes at the workload's cache length (the prompt's rows).
+    assert line["config"] == bench.batch1_config("fp32-2layer", bench.CONFIGS["fp32-2layer"], 1)
+    assert f"threads x ({bench.CONFIGS['fp32-2layer']['prompt']} cached rows" in line["cpu_baseline"]["sample"]
+
+
+def test_reference_context_per_configuration():
+    assert bench.ref_context(bench.CONFIGS["fp32-ctx512"]) == 512
+    assert bench.ref_context(bench.CONFIGS["bf16-ctx4096"]) == 4096
+    assert bench.ref_context(bench.CONFIGS["bf16-batch64"]) == (128 + 8192) // 2
+    kv = bench.context_kv(2, 16)
+    assert len(kv) == 2 and kv[1][0].shape == (2, 16, 128) and kv[1][0].dtype.name == "float32"
 
 
 def test_clock_sampler_window():
